@@ -1,0 +1,441 @@
+"""Benchmark: paged-attention decode µs/call and KV-read TB/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
+
+One step = one decode call over one batch of the workload, inputs resident
+in HBM.  Default workload c5 (the 1/2/4/8-GPU serving batch of the spec:
+256 sequences, 64/8 heads, lengths U[1,32768] with 5% empty, fp16, vLLM
+layout, 16 GB of KV); at N GPUs (torchrun, one rank per GPU) every rank owns
+8/N KV heads and their pages, so total work is fixed ("strong" scaling).
+Other workloads (c1..c4) are available with --workload.
+
+Printed (rank 0, one JSON line): value = aggregate KV-read TB/s over all
+ranks (KV bytes of the whole batch / max-over-ranks device time), the
+µs/call, the roofline of the partition kernel against the measured HBM
+copy bandwidth, the CPU baseline (the oracle's C port on this host's cores,
+bounded sample), the end-to-end number through the public API with pinned
+host buffers, clocks sampled by NVML during the timed region, and the number
+of this library's kernel launches in the timed region.
+
+--impl reference times the reference's CPU implementation (restated by the
+oracle's multithreaded C port; the reference has no other CPU path) on a
+bounded sample of the same workload on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-attn decode KV-read TB/s (µs/call; % HBM peak) at N B200"
+UNIT = "TB/s"
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _profile_traffic(workload: str) -> float | None:
+    """Per-launch DRAM bytes of the partition kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / f"traffic_{workload}.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+class ClockSampler:
+    """NVML sampling of SM clocks and throttle reasons in a background thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clocks_setting": 0x100,
+    }
+
+    def __init__(self, indices, interval=0.01):
+        self.samples = []
+        self.interval = interval
+        self._stop = threading.Event()
+        self._thread = None
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in indices]
+            self.max_mhz = max(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in self._handles)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            for h in self._handles:
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((time.perf_counter(), mhz, int(reasons)))
+                except Exception:  # noqa: BLE001
+                    pass
+            time.sleep(self.interval)
+
+    def start(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self, t0, t1) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "NVML unavailable"}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        used = inside if inside else self.samples[-3:]
+        reasons = set()
+        for _, _, r in used:
+            for name, bit in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    reasons.add(name)
+        mhz = statistics.median(s[1] for s in used) if used else None
+        out = {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons), "samples": len(inside)}
+        if not inside:
+            out["note"] = "timed region shorter than the sampling interval; nearest samples used"
+        return out
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, ws, local
+
+
+# ---------------------------------------------------------------------------
+# CPU (reference) arm
+# ---------------------------------------------------------------------------
+def _cpu_sample(workload: str, target_bytes: float):
+    """Sequences of the workload (chosen by a seeded draw over the non-empty
+    ones) adding up to ~target_bytes of KV, materialised on the host."""
+    import torch
+
+    from decodekernels_b200 import workloads
+
+    lens = workloads.seq_lens(workload)
+    c = workloads.CONFIGS[workload]
+    per_tok = c.num_kv_heads * c.head_dim * 2 * (torch.finfo(c.dtype).bits // 8)
+    order = torch.randperm(len(lens), generator=torch.Generator().manual_seed(11)).tolist()
+    chosen, total = [], 0
+    for i in order:
+        if lens[i] <= 0:
+            continue
+        chosen.append(i)
+        total += lens[i] * per_tok
+        if total >= target_bytes:
+            break
+    batch = workloads.make(workload, "cpu", seqs=sorted(chosen))
+    return batch
+
+
+def workloads_lens(workload: str) -> list[int]:
+    from decodekernels_b200 import workloads
+
+    return workloads.seq_lens(workload)
+
+
+def cpu_throughput(workload: str, seconds: float, target_bytes: float = 256e6, steps: int | None = None,
+                   warmup: int = 0):
+    """Time the oracle's C port (all host threads) on a bounded sample."""
+    from oracle import native
+
+    b = _cpu_sample(workload, target_bytes)
+    args = (b.q, b.kv.k_cache, b.kv.v_cache, b.kv.block_tables, b.kv.seq_lens)
+    for _ in range(warmup):
+        native.dense_c(*args)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and (time.perf_counter() < t_end or not times)) or (steps is not None and len(times) < steps):
+        t = time.perf_counter()
+        native.dense_c(*args)
+        times.append(time.perf_counter() - t)
+    per_call = statistics.median(times)
+    kvb = b.kv_bytes()
+    return {
+        "value": kvb / per_call / 1e12,
+        "unit": UNIT,
+        "cores": native.max_threads(),
+        "kind": "port",
+        "sample": f"{len(b.lens)} of {len(workloads_lens(workload))} sequences of {workload} "
+                  f"({sum(b.lens)} tokens, {kvb / 1e6:.0f} MB KV), median of {len(times)} calls of the oracle's "
+                  f"C port (OpenMP, all host threads)",
+        "seconds_per_call": per_call,
+        "calls": len(times),
+    }
+
+
+def run_reference_arm(args) -> None:
+    rank, world, _ = _dist()
+    if rank != 0:
+        return
+    from oracle import build as obuild
+
+    obuild.build_oracle()
+    # each step is one oracle call over a ~64 MB sample so K + W steps stay within minutes
+    res = cpu_throughput(args.workload, 0, target_bytes=64e6, steps=args.steps, warmup=args.warmup)
+    v = res["value"]
+    line = {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["seconds_per_call"] * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.workload, "sample": res["sample"]},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": res["cores"], "kind": "port", "sample": res["sample"]},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def _check_parity(batch, out, rank) -> dict:
+    """Compare a few sequences of the call's output with the C oracle."""
+    import numpy as np
+
+    from decodekernels_b200 import workloads
+    from oracle import native
+
+    lens = batch.lens
+    live = [i for i, L in enumerate(lens) if L > 0]
+    pick = sorted(set([live[0], max(live, key=lambda i: lens[i]), min(live, key=lambda i: lens[i])]
+                      + [i for i, L in enumerate(lens) if L == 0][:1]))
+    q, kv = workloads.compact_sequences(batch, pick)
+    ref = native.dense_c(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens)
+    got = out[pick].float().cpu().numpy()
+    err = np.abs(got - ref)
+    ok = bool(np.isfinite(got).all() and err.max() <= 2e-2 and err.mean() <= 2e-3)
+    if not ok:
+        raise SystemExit(f"rank {rank}: parity check failed before timing (max-abs {err.max():.3e}, "
+                         f"mean-abs {err.mean():.3e}) on sequences {pick}")
+    return {"sequences": pick, "max_abs": float(err.max()), "mean_abs": float(err.mean())}
+
+
+def run_gpu_arm(args) -> None:
+    import torch
+
+    rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    import decodekernels_b200 as dk
+    from decodekernels_b200 import capi, workloads
+
+    if not dk.is_available():
+        raise SystemExit(f"decodekernels_b200 native library unavailable: {dk.ops._IMPORT_ERROR}")
+
+    batch = workloads.make(args.workload, dev, shard=(rank, world))
+    q, kv = batch.q, batch.kv
+    n, hq, d = q.shape
+    max_len = batch.max_seq_len
+    out = torch.empty_like(q)
+    ws = dk.alloc_workspace(n, hq, d, max_len, dev, num_kv_heads=kv.k_cache.shape[2],
+                            block_size=kv.block_size)
+    plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, ws)
+
+    def step():
+        dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=max_len,
+                                  out=out, workspace=ws)
+
+    step()
+    torch.cuda.synchronize()
+    parity = _check_parity(batch, out, rank)
+
+    l2_bytes = 126 * 1024 * 1024
+    flush = batch.kv_bytes() < 4 * l2_bytes
+    flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev) if flush else None
+
+    sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        if flush:
+            flush_buf.zero_()
+        step()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        if flush:
+            flush_buf.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    t1 = time.perf_counter()
+    per_step = [s.elapsed_time(e) * 1e-3 for s, e in zip(starts, ends)]  # seconds, kernels only
+    device_s = sum(per_step)
+    if sampler:
+        sampler.stop()
+
+    # End to end through the public API with pinned host buffers: H2D of q,
+    # block tables and lengths, the call, D2H of the output, every step.
+    h_q = q.cpu().pin_memory()
+    h_bt = kv.block_tables.cpu().pin_memory()
+    h_sl = kv.seq_lens.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = h_q.numel() * h_q.element_size() + h_bt.numel() * 4 + h_sl.numel() * 4
+    d2h = h_out.numel() * h_out.element_size()
+    q_dev, bt_dev, sl_dev = torch.empty_like(q), torch.empty_like(kv.block_tables), torch.empty_like(kv.seq_lens)
+
+    def e2e_step():
+        q_dev.copy_(h_q, non_blocking=True)
+        bt_dev.copy_(h_bt, non_blocking=True)
+        sl_dev.copy_(h_sl, non_blocking=True)
+        dk.paged_attention_decode(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=max_len, out=out,
+                                  workspace=ws)
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    e_steps = max(10, min(args.steps, 100))
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e_steps):
+        if flush:
+            flush_buf.zero_()
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize()
+    e2e_s = es.elapsed_time(ee) * 1e-3
+    if flush:  # remove the flush time from the end-to-end window
+        fs, fe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fs.record(stream)
+        for _ in range(e_steps):
+            flush_buf.zero_()
+        fe.record(stream)
+        torch.cuda.synchronize()
+        e2e_s -= fs.elapsed_time(fe) * 1e-3
+
+    kv_local = batch.kv_bytes()
+    alg_local = batch.algorithmic_bytes()
+    stats = torch.tensor([device_s, e2e_s, float(kv_local), float(alg_local)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        tmax = stats[:2].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        sums = stats[2:].clone()
+        dist.all_reduce(sums, op=dist.ReduceOp.SUM)
+        device_s, e2e_s = tmax.tolist()
+        kv_total, alg_total = sums.tolist()
+    else:
+        kv_total, alg_total = float(kv_local), float(alg_local)
+
+    if rank == 0:
+        step_s = device_s / args.steps
+        value = kv_total / step_s / 1e12
+        peaks = _peaks()
+        # roofline of this rank's launches: algorithmic bytes per call / mean call time
+        local_step = sum(per_step) / len(per_step)
+        achieved = alg_local / local_step / 1e9
+        traffic = _profile_traffic(args.workload) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "us_per_call": step_s * 1e6,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16" if
+            batch.config.dtype == torch.float16 else "bf16", "accumulate": "f32", "data": "synthetic",
+            "impl": "ours",
+            "config": {
+                "workload": f"{args.workload}: {batch.config.description}",
+                "num_seqs": n, "num_q_heads": batch.config.num_q_heads, "num_kv_heads": batch.config.num_kv_heads,
+                "head_dim": d, "block_size": kv.block_size, "max_seq_len": max_len,
+                "kv_bytes_total": kv_total, "algorithmic_bytes_total": alg_total,
+                "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                "l2": "L2 flushed (256 MB write) before every step" if flush else
+                      "inputs larger than L2 (no flush between steps)",
+                "plan": plan, "parity": parity,
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                "peak_source": f"{peaks['source']} HBM copy bandwidth",
+                "note": "achieved = algorithmic bytes per call / CUDA-event time of the whole call "
+                        "(partition + merge kernels)",
+            },
+            "e2e": {"value": kv_total / (e2e_s / e_steps) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e_steps, "api": "decodekernels_b200.paged_attention_decode"},
+            "gpu_launches": args.steps * plan["launches"],
+            "clocks": sampler.summary(t0, t1) if sampler else None,
+            "wall_s_timed": t1 - t0,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_throughput(args.workload, seconds=args.cpu_seconds)
+            line["cpu_baseline"].pop("calls", None)
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    _, world, _ = _dist()
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

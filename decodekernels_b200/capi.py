@@ -1,0 +1,205 @@
+"""ctypes bindings of the C ABI (``include/dk_paged_attention.h``).
+
+This is the torch-free boundary: every call passes raw device pointers and
+element strides to ``libdk_b200.so``.  The helpers here take torch tensors
+only to read their pointers, shapes and strides; tests use them to drive the
+C ABI directly (including options the torch op does not expose: a fixed
+partition size, the CUDA-core path).
+
+The library is loaded from ``decodekernels_b200/lib/``; if it is missing,
+``load()`` raises -- there is no fallback implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdk_b200.so"
+
+DK_DTYPE_FLOAT16 = 0
+DK_DTYPE_BFLOAT16 = 1
+DK_PATH_NONE, DK_PATH_TMA_MMA, DK_PATH_SIMT = 0, 1, 2
+DK_FLAG_FORCE_SIMT = 1
+DK_MAX_GQA_GROUP = 8
+DK_TILE_TOKENS = 64
+DK_REF_PARTITION_SIZE = 512
+
+EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
+            "dk_device_wait_timeouts", "dk_version")
+
+
+class DkPagedAttnArgs(ctypes.Structure):
+    _fields_ = [
+        ("out", ctypes.c_void_p),
+        ("q", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("v_cache", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("seq_lens", ctypes.c_void_p),
+        ("tmp_out", ctypes.c_void_p),
+        ("max_logits", ctypes.c_void_p),
+        ("exp_sums", ctypes.c_void_p),
+        ("q_stride_seq", ctypes.c_int64),
+        ("q_stride_head", ctypes.c_int64),
+        ("out_stride_seq", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("k_stride_block", ctypes.c_int64),
+        ("k_stride_token", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("v_stride_block", ctypes.c_int64),
+        ("v_stride_token", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("bt_stride", ctypes.c_int64),
+        ("num_seqs", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("num_blocks", ctypes.c_int32),
+        ("max_seq_len", ctypes.c_int32),
+        ("max_partitions", ctypes.c_int32),
+        ("partition_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+    ]
+
+
+class DkPlan(ctypes.Structure):
+    _fields_ = [
+        ("path", ctypes.c_int32),
+        ("partition_size", ctypes.c_int32),
+        ("num_partitions", ctypes.c_int32),
+        ("split", ctypes.c_int32),
+        ("num_ctas", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
+        ("launches", ctypes.c_int32),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load libdk_b200.so (once) and declare the exported signatures."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is not built; run `python -m decodekernels_b200.build`")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.dk_paged_attention_decode.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.c_void_p]
+        lib.dk_paged_attention_decode.restype = ctypes.c_int
+        lib.dk_plan.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.POINTER(DkPlan)]
+        lib.dk_plan.restype = ctypes.c_int
+        lib.dk_num_partitions.argtypes = [ctypes.c_int32] * 6
+        lib.dk_num_partitions.restype = ctypes.c_int32
+        lib.dk_last_error.argtypes = []
+        lib.dk_last_error.restype = ctypes.c_char_p
+        lib.dk_device_wait_timeouts.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]
+        lib.dk_device_wait_timeouts.restype = ctypes.c_int
+        lib.dk_version.argtypes = []
+        lib.dk_version.restype = ctypes.c_int32
+        _lib = lib
+        return lib
+
+
+def last_error() -> str:
+    return load().dk_last_error().decode()
+
+
+def version() -> int:
+    return int(load().dk_version())
+
+
+def num_partitions(num_seqs: int, num_kv_heads: int, head_dim: int, block_size: int, max_seq_len: int,
+                   device: int = -1) -> int:
+    n = load().dk_num_partitions(num_seqs, num_kv_heads, head_dim, block_size, max_seq_len, device)
+    if n < 0:
+        raise ValueError(f"dk_num_partitions rejected ({num_seqs}, {num_kv_heads}, {head_dim}, {max_seq_len})")
+    return int(n)
+
+
+def wait_timeouts(device: int = 0) -> int:
+    count = ctypes.c_uint32(0)
+    rc = load().dk_device_wait_timeouts(device, ctypes.byref(count))
+    if rc != 0:
+        raise RuntimeError(f"dk_device_wait_timeouts failed ({rc}): {last_error()}")
+    return int(count.value)
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.float16:
+        return DK_DTYPE_FLOAT16
+    if t.dtype == torch.bfloat16:
+        return DK_DTYPE_BFLOAT16
+    return -1
+
+
+def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
+              partition_size: int = 0, force_simt: bool = False) -> DkPagedAttnArgs:
+    """Fill the C struct from tensors (pointers + element strides)."""
+    a = DkPagedAttnArgs()
+    a.out = out.data_ptr()
+    a.q = q.data_ptr()
+    a.k_cache = k_cache.data_ptr()
+    a.v_cache = v_cache.data_ptr()
+    a.block_tables = block_tables.data_ptr()
+    a.seq_lens = seq_lens.data_ptr()
+    if workspace is not None and workspace[0].numel() > 0:
+        tmp_out, max_logits, exp_sums = workspace
+        a.tmp_out, a.max_logits, a.exp_sums = tmp_out.data_ptr(), max_logits.data_ptr(), exp_sums.data_ptr()
+        a.max_partitions = tmp_out.shape[2]
+    a.q_stride_seq, a.q_stride_head = q.stride(0), q.stride(1)
+    a.out_stride_seq, a.out_stride_head = out.stride(0), out.stride(1)
+    a.k_stride_block, a.k_stride_token, a.k_stride_head = k_cache.stride()[:3]
+    a.v_stride_block, a.v_stride_token, a.v_stride_head = v_cache.stride()[:3]
+    a.bt_stride = block_tables.stride(0)
+    a.num_seqs, a.num_q_heads, a.head_dim = q.shape
+    a.num_kv_heads = k_cache.shape[2]
+    a.block_size = k_cache.shape[1]
+    a.num_blocks = k_cache.shape[0]
+    a.max_seq_len = int(max_seq_len)
+    a.partition_size = int(partition_size)
+    a.dtype = _dtype_code(q)
+    a.flags = DK_FLAG_FORCE_SIMT if force_simt else 0
+    a.scale = float(scale)
+    return a
+
+
+def plan(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
+         partition_size: int = 0, force_simt: bool = False) -> dict:
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
+                  force_simt)
+    p = DkPlan()
+    rc = load().dk_plan(ctypes.byref(a), ctypes.byref(p))
+    if rc != 0:
+        raise RuntimeError(f"dk_plan failed ({rc}): {last_error()}")
+    return p.as_dict()
+
+
+def decode(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
+           partition_size: int = 0, force_simt: bool = False, stream=None) -> int:
+    """dk_paged_attention_decode on ``stream`` (default: torch's current stream).
+
+    Returns 0; raises RuntimeError with the library's message otherwise."""
+    import torch
+
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
+                  force_simt)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
+    rc = load().dk_paged_attention_decode(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_paged_attention_decode failed ({rc}): {last_error()}")
+    return rc

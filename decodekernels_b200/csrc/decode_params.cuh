@@ -1,0 +1,49 @@
+// Parameters shared by the partition kernels and the merge kernel.
+#pragma once
+
+#include <stdint.h>
+
+namespace dkb {
+
+constexpr int kTileTokens = 64;      // tokens per pipeline stage (one CTA-wide tile)
+constexpr int kSubTokens = 16;       // tokens per consumer warp per tile (mma M)
+constexpr int kConsumerWarps = 4;    // kTileTokens / kSubTokens
+constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
+constexpr int kSimtThreads = 128;
+constexpr int kMergeThreads = 256;
+constexpr int kMaxGroup = 8;         // query heads per KV head (mma N)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Everything a launch needs besides the TMA descriptors.  Strides are in
+// elements.  Field meanings follow DecodeKernels' PagedAttnParams
+// (csrc/paged_attention.cuh:39-58) plus the planner's outputs.
+struct DecodeParams {
+  void* out;
+  const void* q;
+  const void* k_cache;  // read directly by the CUDA-core path only
+  const void* v_cache;
+  const int* block_tables;
+  const int* seq_lens;
+  float* tmp_out;
+  float* max_logits;
+  float* exp_sums;
+  int64_t q_stride_seq, q_stride_head;
+  int64_t out_stride_seq, out_stride_head;
+  int64_t k_stride_block, k_stride_token, k_stride_head;
+  int64_t v_stride_block, v_stride_token, v_stride_head;
+  int64_t bt_stride;
+  int num_q_heads;
+  int group;           // num_q_heads / num_kv_heads
+  int block_size;
+  int num_blocks;      // cache blocks; ids outside [0, num_blocks) read as zeros
+  int rows_per_op;     // token rows per TMA box: min(block_size, kTileTokens)
+  int partition_size;  // tokens per partition, a multiple of kTileTokens
+  int num_partitions;  // partitions in the grid
+  int ws_partitions;   // workspace row stride (capacity)
+  int split;           // 1: partitions write the workspace and the merge kernel writes out
+  int slot_head, slot_tok, slot_blk;  // tensor-map coordinate slot (1..3) of each cache dim
+  float scale_log2;    // softmax scale * log2(e)
+};
+
+}  // namespace dkb

@@ -1,0 +1,90 @@
+// Log-sum-exp merge of split-K partitions (DecodeKernels'
+// paged_attention_reduce_kernel, csrc/paged_attention.cuh:227-269):
+//   M = max_i m_i,  w_i = s_i exp(m_i - M),  out = sum_i w_i o_i / sum_i w_i
+// over the live partitions num_parts = min(ceil(L / partition_size), P);
+// zeros when L <= 0.
+//
+// One CTA of 8 warps per (q_head, seq).  Warp w folds partitions w, w+8, ...
+// with each lane holding head_dim / 32 consecutive floats of the partial
+// output (one 8/16/32-byte load per partition, unrolled so several
+// partitions are in flight), then the warps are summed through shared memory.
+// Launched with programmatic dependent launch: the CTAs start while the
+// partition kernel drains and wait for its results in griddepcontrol.wait.
+#pragma once
+
+#include "decode_params.cuh"
+#include "dk_ptx.cuh"
+
+namespace dkb {
+
+template <int N>
+struct alignas(4 * N) F32Vec {
+  float v[N];
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const DecodeParams p) {
+  constexpr int WARPS = kMergeThreads / 32;
+  constexpr int V = D / 32;
+  using Vec = F32Vec<V>;
+  __shared__ float red[WARPS][D];
+  __shared__ float wsum[WARPS];
+  __shared__ float wmax[WARPS];
+
+  const int q_head = blockIdx.x;
+  const int seq = blockIdx.y;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  pdl_wait_primary();
+  T* out = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head;
+  const int seq_len = p.seq_lens[seq];
+  if (seq_len <= 0) {
+    for (int d = threadIdx.x; d < D; d += kMergeThreads) out[d] = Conv<T>::from_f32(0.0f);
+    return;
+  }
+  const int num_parts = min((seq_len + p.partition_size - 1) / p.partition_size, p.num_partitions);
+  const int64_t row0 = (static_cast<int64_t>(seq) * p.num_q_heads + q_head) * p.ws_partitions;
+  const float* ml = p.max_logits + row0;
+  const float* es = p.exp_sums + row0;
+  const float* tmp = p.tmp_out + row0 * D;
+
+  float M = -INFINITY;
+  for (int i = threadIdx.x; i < num_parts; i += kMergeThreads) M = fmaxf(M, ml[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) wmax[warp] = M;
+  __syncthreads();
+  M = wmax[0];
+#pragma unroll
+  for (int w = 1; w < WARPS; ++w) M = fmaxf(M, wmax[w]);
+
+  float acc[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) acc[j] = 0.0f;
+  float ws = 0.0f;
+#pragma unroll 4
+  for (int i = warp; i < num_parts; i += WARPS) {
+    const float w = es[i] * fast_exp2((ml[i] - M) * kLog2e);
+    const Vec x = *reinterpret_cast<const Vec*>(tmp + static_cast<int64_t>(i) * D + lane * V);
+    ws += w;
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = fmaf(w, x.v[j], acc[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < V; ++j) red[warp][lane * V + j] = acc[j];
+  if (lane == 0) wsum[warp] = ws;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < WARPS; ++w) total += wsum[w];
+  const float inv = 1.0f / total;
+  for (int d = threadIdx.x; d < D; d += kMergeThreads) {
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < WARPS; ++w) o += red[w][d];
+    out[d] = Conv<T>::from_f32(o * inv);
+  }
+}
+
+}  // namespace dkb

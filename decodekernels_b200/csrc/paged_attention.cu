@@ -1,0 +1,510 @@
+// libdk_b200: paged-attention decode for B200 (sm_100a) behind a C ABI
+// (include/dk_paged_attention.h).
+//
+// Host side of the library: argument validation (the checks DecodeKernels
+// makes in csrc/ops.cu:48-106 and csrc/paged_attention.cuh:315-322), the
+// per-shape planner (partition size, grid, path), TMA descriptor
+// construction, and the launches (partition kernel, then the merge kernel
+// when the plan splits), both with programmatic dependent launch so their
+// prologues overlap the previous kernel's tail.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/dk_paged_attention.h"
+#include "decode_params.cuh"
+#include "merge_partitions.cuh"
+#include "partition_simt.cuh"
+#include "partition_tma.cuh"
+
+namespace dkb {
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMinPartition = 128;
+constexpr int kMaxPartition = 512;
+constexpr int kWaves = 4;  // planner target: ~4 resident waves of partition CTAs
+
+thread_local char g_last_error[512] = {0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(static_cast<int>(e), "%s: %s", what, cudaGetErrorString(e));
+}
+
+constexpr int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+constexpr int round_up(long long a, long long b) { return static_cast<int>(((a + b - 1) / b) * b); }
+
+template <int D>
+constexpr int tma_stages() {
+  return D == 64 ? 4 : 3;
+}
+
+// Resident partition CTAs per SM on the TMA path (shared memory bound).
+int tma_ctas_per_sm(int D) { return D == 64 ? 3 : (D == 128 ? 2 : 1); }
+
+int smem_for(int path, int D) {
+  if (path == DK_PATH_TMA_MMA) {
+    switch (D) {
+      case 64: return TmaConfig<64, tma_stages<64>()>::kSmemBytes;
+      case 128: return TmaConfig<128, tma_stages<128>()>::kSmemBytes;
+      default: return TmaConfig<256, tma_stages<256>()>::kSmemBytes;
+    }
+  }
+  switch (D) {
+    case 64: return SimtConfig<64>::kSmemBytes;
+    case 128: return SimtConfig<128>::kSmemBytes;
+    default: return SimtConfig<256>::kSmemBytes;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-device facts, cached
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mu;
+int g_num_sms[kMaxDevices] = {0};
+
+int num_sms(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    g_num_sms[dev] = n;
+  }
+  return g_num_sms[dev];
+}
+
+// Opt every kernel that needs more than 48 KB of dynamic shared memory in,
+// once per (kernel, device).
+template <typename Kernel>
+cudaError_t ensure_smem_attr(Kernel kernel, int smem, int dev, bool* done) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (dev >= 0 && dev < kMaxDevices && done[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev] = true;
+  return e;
+}
+
+// ---------------------------------------------------------------------------
+// Validation (DecodeKernels csrc/ops.cu:48-106, csrc/paged_attention.cuh:315-322)
+// ---------------------------------------------------------------------------
+bool aligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+int validate(const DkPagedAttnArgs* a) {
+  if (a == nullptr) return fail(1, "dk_paged_attention_decode: args is NULL");
+  if (a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
+    return fail(1, "paged_attention_decode: expected float16 or bfloat16 (dtype code %d)", a->dtype);
+  if (a->num_seqs < 0 || a->num_seqs > 65535) return fail(1, "num_seqs must be in [0, 65535]");
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(1, "head_dim must be 64, 128 or 256, got %d", a->head_dim);
+  if (a->num_kv_heads <= 0 || a->num_q_heads <= 0 || a->num_q_heads % a->num_kv_heads != 0)
+    return fail(1, "num_q_heads must be a multiple of num_kv_heads");
+  if (a->num_q_heads / a->num_kv_heads > DK_MAX_GQA_GROUP)
+    return fail(1, "GQA group size above %d is not supported", DK_MAX_GQA_GROUP);
+  if (a->block_size <= 0) return fail(1, "block_size must be positive");
+  if (a->max_seq_len < 0) return fail(1, "max_seq_len must be non-negative");
+  if (a->max_partitions < 0) return fail(1, "max_partitions must be non-negative");
+  if (a->partition_size < 0 || a->partition_size % DK_TILE_TOKENS != 0)
+    return fail(1, "partition_size must be 0 (planner) or a positive multiple of %d", DK_TILE_TOKENS);
+  if (a->num_seqs == 0) return 0;
+  if (!a->out || !a->q || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens)
+    return fail(1, "paged_attention_decode: NULL tensor pointer");
+  if (a->num_blocks <= 0) return fail(1, "num_blocks must be positive");
+  // Vectorised row loads: head_dim / 32 elements per lane (csrc/ops.cu:72-79).
+  const int64_t vec = a->head_dim / 32;
+  const int64_t strides[6] = {a->k_stride_block, a->k_stride_token, a->k_stride_head,
+                              a->v_stride_block, a->v_stride_token, a->v_stride_head};
+  for (int64_t s : strides) {
+    if (s < 0 || s % vec != 0) return fail(1, "KV-cache strides must be multiples of head_dim / 32 for vectorised loads");
+  }
+  if (!aligned(a->k_cache, static_cast<size_t>(vec * 2)) || !aligned(a->v_cache, static_cast<size_t>(vec * 2)))
+    return fail(1, "KV-cache pointers must be aligned to head_dim / 16 bytes");
+  if (a->max_partitions > 0 && (!a->tmp_out || !a->max_logits || !a->exp_sums))
+    return fail(1, "split-K workspace pointers are NULL but max_partitions > 0");
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Planner
+// ---------------------------------------------------------------------------
+// Tokens per partition before workspace constraints: split until the grid
+// holds ~kWaves waves of resident CTAs, in partitions of 128..512 tokens.
+int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms) {
+  const long long pairs = std::max<long long>(1, static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1));
+  const long long target = static_cast<long long>(kWaves) * sms * tma_ctas_per_sm(head_dim);
+  const long long want = std::max<long long>(1, (target + pairs - 1) / pairs);
+  int ps = round_up(ceil_div(max_seq_len, want), DK_TILE_TOKENS);
+  return std::min(std::max(ps, kMinPartition), kMaxPartition);
+}
+
+// Path choice: the TMA path needs 16-byte aligned bases and strides (the
+// tensor-map rules) and a block size that tiles the 64-token stage.
+bool tma_eligible(const DkPagedAttnArgs& a) {
+  if (a.flags & DK_FLAG_FORCE_SIMT) return false;
+  const int bs = a.block_size;
+  if (bs < 8) return false;
+  if (!((bs <= DK_TILE_TOKENS && DK_TILE_TOKENS % bs == 0) || bs % DK_TILE_TOKENS == 0)) return false;
+  if (!aligned(a.k_cache, 16) || !aligned(a.v_cache, 16)) return false;
+  const int64_t sizes[3] = {a.num_blocks, a.block_size, a.num_kv_heads};
+  const int64_t ks[3] = {a.k_stride_block, a.k_stride_token, a.k_stride_head};
+  const int64_t vs[3] = {a.v_stride_block, a.v_stride_token, a.v_stride_head};
+  for (int i = 0; i < 3; ++i) {
+    if (sizes[i] <= 1) continue;  // the coordinate is always 0; the stride is never used
+    if ((ks[i] * 2) % 16 != 0 || (vs[i] * 2) % 16 != 0) return false;
+    if (ks[i] * 2 >= (int64_t(1) << 40) || vs[i] * 2 >= (int64_t(1) << 40)) return false;
+  }
+  return true;
+}
+
+void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
+  std::memset(pl, 0, sizeof(*pl));
+  if (a.num_seqs == 0) {
+    pl->path = DK_PATH_NONE;
+    return;
+  }
+  pl->path = tma_eligible(a) ? DK_PATH_TMA_MMA : DK_PATH_SIMT;
+  const int L = a.max_seq_len;
+  int ps, parts;
+  if (L <= 0) {
+    ps = DK_TILE_TOKENS;
+    parts = 1;
+  } else if (a.max_partitions <= 0) {
+    ps = round_up(L, DK_TILE_TOKENS);  // no workspace: one pass over the whole sequence
+    parts = 1;
+  } else {
+    ps = a.partition_size > 0 ? a.partition_size
+                              : desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L, num_sms(dev));
+    parts = ceil_div(L, ps);
+    if (parts > a.max_partitions) {  // the caller's workspace caps the partition count
+      ps = round_up(ceil_div(L, a.max_partitions), DK_TILE_TOKENS);
+      parts = ceil_div(L, ps);
+    }
+  }
+  pl->partition_size = ps;
+  pl->num_partitions = parts;
+  pl->split = parts > 1 ? 1 : 0;
+  pl->num_ctas = static_cast<int32_t>(std::min<long long>(INT_MAX, 1LL * parts * a.num_kv_heads * a.num_seqs));
+  pl->stages = pl->path == DK_PATH_TMA_MMA ? (a.head_dim == 64 ? 4 : 3) : 0;
+  pl->smem_bytes = smem_for(pl->path, a.head_dim);
+  pl->launches = pl->split ? 2 : 1;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    } else {
+      cudaGetLastError();
+    }
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int64_t strides[3];
+  int64_t sizes[3];
+  int rows;
+  int head_dim;
+  int dev;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  int slot_head, slot_tok, slot_blk;
+  bool used;
+};
+
+constexpr int kMapCache = 32;
+std::mutex g_map_mu;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+
+// 4-D map over one cache view: dim 0 = head_dim (contiguous), dims 1..3 =
+// {head, token, block} ordered by increasing stride.  The box is one
+// 64-column half of `rows` token rows of one head of one page, 128-byte
+// swizzled.  Writes each dim's coordinate slot.
+int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, int64_t num_blocks, int block_size,
+              int num_kv_heads, int head_dim, int rows, int dev, CUtensorMap* out, int* slot_head, int* slot_tok,
+              int* slot_blk) {
+  MapKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.ptr = ptr;
+  key.strides[0] = s_head;
+  key.strides[1] = s_tok;
+  key.strides[2] = s_block;
+  key.sizes[0] = num_kv_heads;
+  key.sizes[1] = block_size;
+  key.sizes[2] = num_blocks;
+  key.rows = rows;
+  key.head_dim = head_dim;
+  key.dev = dev;
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    for (auto& e : g_maps) {
+      if (e.used && e.key == key) {
+        *out = e.map;
+        *slot_head = e.slot_head;
+        *slot_tok = e.slot_tok;
+        *slot_blk = e.slot_blk;
+        return 0;
+      }
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(static_cast<int>(cudaErrorNotSupported), "cuTensorMapEncodeTiled is unavailable");
+
+  // dims 0..2 of the sort: 0 = head, 1 = token, 2 = block
+  int64_t size[3] = {num_kv_heads, block_size, num_blocks};
+  int64_t stride[3] = {s_head, s_tok, s_block};
+  for (int i = 0; i < 3; ++i) {
+    if (size[i] <= 1) stride[i] = 16 / 2;  // never stepped; any legal stride will do
+  }
+  int order[3] = {0, 1, 2};
+  std::sort(order, order + 3, [&](int x, int y) { return stride[x] != stride[y] ? stride[x] < stride[y] : x < y; });
+  cuuint64_t gdim[4];
+  cuuint64_t gstride[3];
+  cuuint32_t box[4];
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  gdim[0] = static_cast<cuuint64_t>(head_dim);
+  box[0] = 64;
+  int slots[3] = {0, 0, 0};
+  for (int k = 0; k < 3; ++k) {
+    const int which = order[k];
+    gdim[k + 1] = static_cast<cuuint64_t>(size[which]);
+    gstride[k] = static_cast<cuuint64_t>(stride[which]) * 2;
+    box[k + 1] = which == 1 ? static_cast<cuuint32_t>(rows) : 1u;
+    slots[which] = k + 1;
+  }
+  CUtensorMap map;
+  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(ptr), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(1, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  *out = map;
+  *slot_head = slots[0];
+  *slot_tok = slots[1];
+  *slot_blk = slots[2];
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  MapEntry& e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.key = key;
+  e.map = map;
+  e.slot_head = slots[0];
+  e.slot_tok = slots[1];
+  e.slot_blk = slots[2];
+  e.used = true;
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Launches
+// ---------------------------------------------------------------------------
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <typename T, int D>
+int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
+  const dim3 grid(static_cast<unsigned>(pl.num_partitions), static_cast<unsigned>(a.num_kv_heads),
+                  static_cast<unsigned>(a.num_seqs));
+  cudaError_t e;
+  if (pl.path == DK_PATH_TMA_MMA) {
+    constexpr int S = tma_stages<D>();
+    static bool attr_done[kMaxDevices] = {false};
+    auto kernel = paged_decode_tma_kernel<T, D, S>;
+    const int smem = TmaConfig<D, S>::kSmemBytes;
+    e = ensure_smem_attr(kernel, smem, dev, attr_done);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(partition kernel)");
+    CUtensorMap kmap, vmap;
+    int sh, st, sb, sh2, st2, sb2;
+    if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
+                          a.num_kv_heads, D, p.rows_per_op, dev, &kmap, &sh, &st, &sb))
+      return r;
+    if (int r = build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks, a.block_size,
+                          a.num_kv_heads, D, p.rows_per_op, dev, &vmap, &sh2, &st2, &sb2))
+      return r;
+    if (sh != sh2 || st != st2 || sb != sb2) {
+      // K and V views order their dims differently: fall back to the CUDA-core kernel.
+      DkPlan simt = pl;
+      simt.path = DK_PATH_SIMT;
+      simt.smem_bytes = SimtConfig<D>::kSmemBytes;
+      return launch_typed<T, D>(a, simt, p, dev, stream);
+    }
+    p.slot_head = sh;
+    p.slot_tok = st;
+    p.slot_blk = sb;
+    e = launch_pdl(kernel, grid, dim3(kTmaThreads), smem, stream, kmap, vmap, p);
+    if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch");
+  } else {
+    auto kernel = paged_decode_simt_kernel<T, D>;
+    e = launch_pdl(kernel, grid, dim3(kSimtThreads), SimtConfig<D>::kSmemBytes, stream, p);
+    if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch (CUDA-core path)");
+  }
+  if (pl.split) {
+    const dim3 mgrid(static_cast<unsigned>(a.num_q_heads), static_cast<unsigned>(a.num_seqs));
+    e = launch_pdl(merge_partitions_kernel<T, D>, mgrid, dim3(kMergeThreads), 0, stream, p);
+    if (e != cudaSuccess) return fail_cuda(e, "merge kernel launch");
+  }
+  return 0;
+}
+
+int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream) {
+  DecodeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.out = a.out;
+  p.q = a.q;
+  p.k_cache = a.k_cache;
+  p.v_cache = a.v_cache;
+  p.block_tables = a.block_tables;
+  p.seq_lens = a.seq_lens;
+  p.tmp_out = pl.split ? a.tmp_out : nullptr;
+  p.max_logits = pl.split ? a.max_logits : nullptr;
+  p.exp_sums = pl.split ? a.exp_sums : nullptr;
+  p.q_stride_seq = a.q_stride_seq;
+  p.q_stride_head = a.q_stride_head;
+  p.out_stride_seq = a.out_stride_seq;
+  p.out_stride_head = a.out_stride_head;
+  p.k_stride_block = a.k_stride_block;
+  p.k_stride_token = a.k_stride_token;
+  p.k_stride_head = a.k_stride_head;
+  p.v_stride_block = a.v_stride_block;
+  p.v_stride_token = a.v_stride_token;
+  p.v_stride_head = a.v_stride_head;
+  p.bt_stride = a.bt_stride;
+  p.num_q_heads = a.num_q_heads;
+  p.group = a.num_q_heads / a.num_kv_heads;
+  p.block_size = a.block_size;
+  p.num_blocks = a.num_blocks;
+  p.rows_per_op = std::min(a.block_size, DK_TILE_TOKENS);
+  p.partition_size = pl.partition_size;
+  p.num_partitions = pl.num_partitions;
+  p.ws_partitions = pl.split ? a.max_partitions : 1;
+  p.split = pl.split;
+  p.scale_log2 = a.scale * kLog2e;
+  const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;
+  switch (a.head_dim) {
+    case 64:
+      return bf16 ? launch_typed<__nv_bfloat16, 64>(a, pl, p, dev, stream) : launch_typed<__half, 64>(a, pl, p, dev, stream);
+    case 128:
+      return bf16 ? launch_typed<__nv_bfloat16, 128>(a, pl, p, dev, stream)
+                  : launch_typed<__half, 128>(a, pl, p, dev, stream);
+    default:
+      return bf16 ? launch_typed<__nv_bfloat16, 256>(a, pl, p, dev, stream)
+                  : launch_typed<__half, 256>(a, pl, p, dev, stream);
+  }
+}
+
+}  // namespace
+}  // namespace dkb
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+int dk_paged_attention_decode(const DkPagedAttnArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate(args)) return e;
+  if (args->num_seqs == 0) return 0;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  DkPlan pl;
+  dkb::make_plan(*args, dev, &pl);
+  if (pl.split && args->max_partitions < pl.num_partitions)
+    return dkb::fail(1, "split-K workspace too small: %d partitions needed", pl.num_partitions);
+  return dkb::launch(*args, pl, dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan) {
+  if (plan == nullptr) return dkb::fail(1, "dk_plan: plan is NULL");
+  if (int e = dkb::validate(args)) return e;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  dkb::make_plan(*args, dev, plan);
+  return 0;
+}
+
+int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                          int32_t max_seq_len, int32_t device) {
+  (void)block_size;
+  if (num_seqs < 0 || max_seq_len < 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256)) return -1;
+  if (max_seq_len == 0) return 1;
+  int dev = device;
+  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = -1;
+  }
+  const int ps = dkb::desired_partition_size(num_seqs, num_kv_heads <= 0 ? 1 : num_kv_heads, head_dim, max_seq_len,
+                                             dkb::num_sms(dev));
+  return dkb::ceil_div(max_seq_len, ps);
+}
+
+const char* dk_last_error(void) { return dkb::g_last_error; }
+
+int dk_device_wait_timeouts(int32_t device, uint32_t* count) {
+  if (count == nullptr) return dkb::fail(1, "dk_device_wait_timeouts: count is NULL");
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return dkb::fail_cuda(e, "cudaGetDevice");
+  if (device >= 0 && device != prev && (e = cudaSetDevice(device)) != cudaSuccess)
+    return dkb::fail_cuda(e, "cudaSetDevice");
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, dkb::g_wait_timeouts, sizeof(v));
+  if (device >= 0 && device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return dkb::fail_cuda(e, "cudaMemcpyFromSymbol");
+  *count = v;
+  return 0;
+}
+
+int32_t dk_version(void) { return dkb::kVersion; }
+
+}  // extern "C"

@@ -1,0 +1,155 @@
+// torch.ops.decode_kernels.paged_attention_decode: the drop-in torch op.
+//
+// Same schema as DecodeKernels (csrc/ops.cu:271-273), registered for the
+// CUDA dispatch key (csrc/ops.cu:280-281), with the same argument checks and
+// error texts (csrc/ops.cu:48-106).  Tensors are turned into plain pointers
+// and element strides and handed to the C ABI (dk_paged_attention_decode in
+// libdk_b200.so), which launches on the current CUDA stream of q's device.
+//
+// Workspace: a split-K workspace is required when max_seq_len > 512 (the
+// reference's rule); a non-empty, well-formed workspace is used at any
+// max_seq_len, so the per-shape planner may also split short batches.
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include "../../include/dk_paged_attention.h"
+
+namespace {
+
+void check_same(const at::Tensor& a, const at::Tensor& b, const char* what) {
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), what, ": dtype mismatch (", a.scalar_type(), " vs ",
+              b.scalar_type(), ")");
+  TORCH_CHECK(a.device() == b.device(), what, ": tensors must be on the same device");
+}
+
+// Checks of csrc/ops.cu:92-104.  Returns an empty string when the workspace is
+// usable, else the reference's error text.
+std::string workspace_problem(const at::Tensor& tmp_out, const at::Tensor& max_logits, const at::Tensor& exp_sums,
+                              int64_t num_seqs, int64_t num_q_heads, int64_t head_dim, int64_t needed_parts) {
+  if (!(tmp_out.scalar_type() == at::kFloat && max_logits.scalar_type() == at::kFloat &&
+        exp_sums.scalar_type() == at::kFloat))
+    return "split-K workspace tensors must be float32";
+  if (!(tmp_out.is_contiguous() && max_logits.is_contiguous() && exp_sums.is_contiguous()))
+    return "split-K workspace tensors must be contiguous";
+  if (!(tmp_out.dim() == 4 && tmp_out.size(0) == num_seqs && tmp_out.size(1) == num_q_heads &&
+        tmp_out.size(2) >= needed_parts && tmp_out.size(3) == head_dim))
+    return "tmp_out must be [num_seqs, num_q_heads, >= ceil(max_seq_len / 512), head_dim]";
+  if (!(max_logits.sizes() == exp_sums.sizes() && max_logits.dim() == 3 && max_logits.size(0) == num_seqs &&
+        max_logits.size(1) == num_q_heads && max_logits.size(2) == tmp_out.size(2)))
+    return "max_logits / exp_sums must be [num_seqs, num_q_heads, max_partitions]";
+  if (tmp_out.size(2) > INT32_MAX) return "too many workspace partitions";
+  return "";
+}
+
+void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                            const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                            double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
+                            at::Tensor& exp_sums) {
+  TORCH_CHECK(q.is_cuda(), "paged_attention_decode: q must be a CUDA tensor");
+  TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "q and out must be [num_seqs, num_q_heads, head_dim]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4,
+              "k_cache and v_cache must be [num_blocks, block_size, num_kv_heads, head_dim]");
+  check_same(q, out, "q/out");
+  check_same(q, k_cache, "q/k_cache");
+  check_same(q, v_cache, "q/v_cache");
+  TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache shapes differ");
+  TORCH_CHECK(q.scalar_type() == at::kHalf || q.scalar_type() == at::kBFloat16,
+              "paged_attention_decode: expected float16 or bfloat16, got ", q.scalar_type());
+
+  const int64_t num_seqs = q.size(0);
+  const int64_t num_q_heads = q.size(1);
+  const int64_t head_dim = q.size(2);
+  const int64_t block_size = k_cache.size(1);
+  const int64_t num_kv_heads = k_cache.size(2);
+  TORCH_CHECK(k_cache.size(3) == head_dim, "cache head_dim does not match q");
+  TORCH_CHECK(head_dim == 64 || head_dim == 128 || head_dim == 256, "head_dim must be 64, 128 or 256, got ",
+              head_dim);
+  TORCH_CHECK(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "num_q_heads must be a multiple of num_kv_heads");
+  TORCH_CHECK(num_q_heads / num_kv_heads <= DK_MAX_GQA_GROUP, "GQA group size above ", DK_MAX_GQA_GROUP,
+              " is not supported");
+  TORCH_CHECK(q.stride(2) == 1 && out.stride(2) == 1 && k_cache.stride(3) == 1 && v_cache.stride(3) == 1,
+              "head_dim must be the contiguous (innermost) dimension");
+  const int64_t vec = head_dim / 32;
+  for (int d = 0; d < 3; ++d) {
+    TORCH_CHECK(k_cache.stride(d) % vec == 0 && v_cache.stride(d) % vec == 0,
+                "KV-cache strides must be multiples of head_dim / 32 for vectorised loads");
+  }
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % (vec * 2) == 0 &&
+                  reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % (vec * 2) == 0,
+              "KV-cache pointers must be aligned to head_dim / 16 bytes");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.stride(1) == 1,
+              "block_tables must be a 2-D int32 tensor with a contiguous last dimension");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.dim() == 1 && seq_lens.is_contiguous(),
+              "seq_lens must be a contiguous 1-D int32 tensor");
+  TORCH_CHECK(block_tables.size(0) >= num_seqs && seq_lens.size(0) >= num_seqs,
+              "block_tables and seq_lens must have at least num_seqs rows");
+  TORCH_CHECK(max_seq_len >= 0, "max_seq_len must be non-negative");
+  TORCH_CHECK(max_seq_len <= INT32_MAX && num_seqs <= 65535 && k_cache.size(0) <= INT32_MAX,
+              "paged_attention_decode: sizes exceed the supported range");
+
+  // Workspace (csrc/ops.cu:89-106).
+  const int64_t needed = (max_seq_len + DK_REF_PARTITION_SIZE - 1) / DK_REF_PARTITION_SIZE;
+  int32_t max_partitions = 0;
+  if (tmp_out.numel() > 0 || max_seq_len > DK_REF_PARTITION_SIZE) {
+    const std::string problem =
+        workspace_problem(tmp_out, max_logits, exp_sums, num_seqs, num_q_heads, head_dim, std::max<int64_t>(needed, 1));
+    if (max_seq_len > DK_REF_PARTITION_SIZE) TORCH_CHECK(problem.empty(), problem);
+    if (problem.empty()) {
+      TORCH_CHECK(tmp_out.device() == q.device(), "split-K workspace must be on q's device");
+      max_partitions = static_cast<int32_t>(tmp_out.size(2));
+    }
+  }
+  if (num_seqs == 0) return;
+
+  DkPagedAttnArgs a{};
+  a.out = out.data_ptr();
+  a.q = q.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.tmp_out = max_partitions ? tmp_out.data_ptr<float>() : nullptr;
+  a.max_logits = max_partitions ? max_logits.data_ptr<float>() : nullptr;
+  a.exp_sums = max_partitions ? exp_sums.data_ptr<float>() : nullptr;
+  a.q_stride_seq = q.stride(0);
+  a.q_stride_head = q.stride(1);
+  a.out_stride_seq = out.stride(0);
+  a.out_stride_head = out.stride(1);
+  a.k_stride_block = k_cache.stride(0);
+  a.k_stride_token = k_cache.stride(1);
+  a.k_stride_head = k_cache.stride(2);
+  a.v_stride_block = v_cache.stride(0);
+  a.v_stride_token = v_cache.stride(1);
+  a.v_stride_head = v_cache.stride(2);
+  a.bt_stride = block_tables.stride(0);
+  a.num_seqs = static_cast<int32_t>(num_seqs);
+  a.num_q_heads = static_cast<int32_t>(num_q_heads);
+  a.num_kv_heads = static_cast<int32_t>(num_kv_heads);
+  a.head_dim = static_cast<int32_t>(head_dim);
+  a.block_size = static_cast<int32_t>(block_size);
+  a.num_blocks = static_cast<int32_t>(k_cache.size(0));
+  a.max_seq_len = static_cast<int32_t>(max_seq_len);
+  a.max_partitions = max_partitions;
+  a.partition_size = 0;
+  a.dtype = q.scalar_type() == at::kBFloat16 ? DK_DTYPE_BFLOAT16 : DK_DTYPE_FLOAT16;
+  a.flags = 0;
+  a.scale = static_cast<float>(scale);
+
+  const c10::cuda::OptionalCUDAGuard guard(q.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  const int status = dk_paged_attention_decode(&a, reinterpret_cast<dk_stream_t>(stream));
+  TORCH_CHECK(status == 0, "paged_attention_decode failed: ", dk_last_error());
+}
+
+}  // namespace
+
+TORCH_LIBRARY(decode_kernels, m) {
+  m.def(
+      "paged_attention_decode(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
+      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) { m.impl("paged_attention_decode", &paged_attention_decode); }

@@ -1,0 +1,141 @@
+"""Python wrapper of ``torch.ops.decode_kernels.paged_attention_decode``.
+
+Same public surface as DecodeKernels' ``decode_kernels/ops.py:14-116`` for the
+attention path: ``PARTITION_SIZE``, ``MAX_GQA_GROUP``, ``SUPPORTED_HEAD_DIMS``,
+``is_available``, ``num_partitions``, ``alloc_workspace`` and
+``paged_attention_decode`` with the same signature, defaults and errors.  The
+op is mutating (``Tensor!`` arguments), so it can run on preallocated buffers
+inside CUDA graphs.
+
+Differences that stay within the reference's contract:
+
+* ``alloc_workspace`` sizes the split-K workspace for this library's per-shape
+  planner (partitions of 128..512 tokens chosen to fill all SMs), which is
+  never smaller than the reference's ``ceil(max_seq_len / 512)``.  Optional
+  keyword ``num_kv_heads`` sizes it exactly; without it the size covers any
+  head count.
+* A non-empty workspace is also used when ``max_seq_len <= 512`` (small
+  batches split to fill the GPU).
+
+The native library is loaded from ``decodekernels_b200/lib``.  If it is not
+built, ``is_available()`` is False and every op raises; there is no CPU
+fallback.
+"""
+
+from __future__ import annotations
+
+import math
+from pathlib import Path
+
+import torch
+
+from . import capi
+
+PARTITION_SIZE = 512  # the reference's split-K partition; the workspace is never smaller than its ceil(L / 512)
+MAX_GQA_GROUP = capi.DK_MAX_GQA_GROUP
+SUPPORTED_HEAD_DIMS = (64, 128, 256)
+
+TORCH_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdk_b200_torch.so"
+
+try:
+    if not TORCH_LIB_PATH.exists():
+        raise ImportError(f"{TORCH_LIB_PATH} is not built")
+    torch.ops.load_library(str(TORCH_LIB_PATH))  # registers torch.ops.decode_kernels.paged_attention_decode
+    capi.load()
+    _AVAILABLE = True
+    _IMPORT_ERROR: Exception | None = None
+except (ImportError, OSError, RuntimeError) as e:  # native library not built
+    _AVAILABLE = False
+    _IMPORT_ERROR = e
+
+
+def is_available() -> bool:
+    """True when the native library is built and a GPU is visible."""
+    return _AVAILABLE and torch.cuda.is_available()
+
+
+def _require() -> None:
+    if not _AVAILABLE:
+        raise RuntimeError(
+            "decodekernels_b200 native library is not built. Run `python -m decodekernels_b200.build` on a "
+            f"machine with nvcc. Original error: {_IMPORT_ERROR}"
+        )
+
+
+if _AVAILABLE:
+    # Fake (meta) implementation lets torch.compile trace through the op.
+    @torch.library.register_fake("decode_kernels::paged_attention_decode")
+    def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums):
+        return None
+
+
+def num_partitions(max_seq_len: int) -> int:
+    """Partitions of the reference's fixed 512-token split (ops.py:67-68)."""
+    return max(1, math.ceil(max_seq_len / PARTITION_SIZE))
+
+
+def _device_index(device) -> int:
+    d = torch.device(device)
+    if d.type != "cuda":
+        return -1
+    return d.index if d.index is not None else (torch.cuda.current_device() if torch.cuda.is_available() else -1)
+
+
+def alloc_workspace(num_seqs: int, num_q_heads: int, head_dim: int, max_seq_len: int, device, *,
+                    num_kv_heads: int | None = None, block_size: int = 16) -> tuple:
+    """Split-K buffers ``(tmp_out, max_logits, exp_sums)`` for a call with these
+    sizes, or three empty tensors when the call will run single-pass.
+
+    Shapes: ``tmp_out [num_seqs, num_q_heads, P, head_dim]``, the other two
+    ``[num_seqs, num_q_heads, P]``, float32, with ``P`` the planner's partition
+    count (at least the reference's ``ceil(max_seq_len / 512)``).
+    """
+    _require()
+    parts = capi.num_partitions(num_seqs, num_kv_heads or 0, head_dim, block_size, max_seq_len, _device_index(device))
+    parts = max(parts, num_partitions(max_seq_len))
+    if parts <= 1 and max_seq_len <= PARTITION_SIZE:
+        empty = torch.empty(0, dtype=torch.float32, device=device)
+        return empty, empty, empty
+    tmp_out = torch.empty(num_seqs, num_q_heads, parts, head_dim, dtype=torch.float32, device=device)
+    max_logits = torch.empty(num_seqs, num_q_heads, parts, dtype=torch.float32, device=device)
+    exp_sums = torch.empty_like(max_logits)
+    return tmp_out, max_logits, exp_sums
+
+
+def paged_attention_decode(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    max_seq_len: int | None = None,
+    out: torch.Tensor | None = None,
+    workspace: tuple | None = None,
+) -> torch.Tensor:
+    """Single-token decode attention over a paged KV cache.
+
+    q: [num_seqs, num_q_heads, head_dim]; k_cache / v_cache:
+    [num_blocks, block_size, num_kv_heads, head_dim] (any strides on the first
+    three dims); block_tables: [num_seqs, max_blocks] int32; seq_lens:
+    [num_seqs] int32. ``max_seq_len`` must be >= every entry of seq_lens; pass
+    it when known to avoid a device-to-host sync.
+    """
+    _require()
+    num_seqs, num_q_heads, head_dim = q.shape
+    if scale is None:
+        scale = head_dim**-0.5
+    if max_seq_len is None:
+        max_seq_len = int(seq_lens[:num_seqs].max().item()) if num_seqs > 0 else 0
+    if out is None:
+        out = torch.empty_like(q)
+    if workspace is None:
+        kv_heads = k_cache.shape[2] if k_cache.dim() == 4 else None
+        bs = k_cache.shape[1] if k_cache.dim() == 4 else 16
+        workspace = alloc_workspace(num_seqs, num_q_heads, head_dim, max_seq_len, q.device, num_kv_heads=kv_heads,
+                                    block_size=bs)
+    tmp_out, max_logits, exp_sums = workspace
+    torch.ops.decode_kernels.paged_attention_decode(
+        out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits, exp_sums
+    )
+    return out

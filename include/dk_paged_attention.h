@@ -1,0 +1,160 @@
+/*
+ * C ABI of the B200 (sm_100a) paged-attention decode library (libdk_b200.so).
+ *
+ * Plain pointers and sizes only: no torch types cross this boundary.  Every
+ * entry point is thread-safe and allocates nothing; the caller owns every
+ * buffer.  Status codes are cudaError_t values (0 = success,
+ * 1 = cudaErrorInvalidValue for rejected arguments); dk_last_error() returns
+ * a human-readable message for the calling thread's last failure.
+ *
+ * What each entry point replaces in DecodeKernels (paths inside that project):
+ *
+ *   dk_paged_attention_decode  <- dk::launch_paged_attention_decode<T>
+ *                                 (csrc/paged_attention.cuh:309-333), the
+ *                                 launcher behind the torch op
+ *                                 decode_kernels::paged_attention_decode
+ *                                 (csrc/ops.cu:44-144, schema :271-273)
+ *   DkPagedAttnArgs            <- dk::PagedAttnParams (csrc/paged_attention.cuh:39-58)
+ *                                 plus the values the launcher took as
+ *                                 separate arguments (head_dim, max_seq_len)
+ *                                 and the dtype the op dispatched on
+ *                                 (csrc/ops.cu:17-27,139-143)
+ *   dk_num_partitions          <- decode_kernels.ops.num_partitions
+ *                                 (decode_kernels/ops.py:67-68), which sized
+ *                                 the split-K workspace (ops.py:71-80)
+ *   dk_plan                    <- the path / grid choice inside
+ *                                 detail::launch (csrc/paged_attention.cuh:271-305)
+ */
+#ifndef DK_PAGED_ATTENTION_H_
+#define DK_PAGED_ATTENTION_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DK_API __attribute__((visibility("default")))
+#else
+#define DK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; declared here so the header needs no CUDA headers. */
+typedef struct CUstream_st* dk_stream_t;
+
+/* Element type of q, out and the K/V caches. */
+enum { DK_DTYPE_FLOAT16 = 0, DK_DTYPE_BFLOAT16 = 1 };
+
+/* Kernel paths reported by dk_plan. */
+enum {
+  DK_PATH_NONE = 0,    /* nothing to launch (num_seqs == 0) */
+  DK_PATH_TMA_MMA = 1, /* TMA-staged pages + tensor-core QK^T / PV (the fast path) */
+  DK_PATH_SIMT = 2     /* plain vector loads + CUDA-core math, for layouts TMA cannot describe */
+};
+
+/* Bits of DkPagedAttnArgs.flags. */
+enum {
+  DK_FLAG_FORCE_SIMT = 1 /* take the CUDA-core path even when the TMA path is eligible (testing) */
+};
+
+/* Limits shared with the Python wrapper. */
+#define DK_MAX_GQA_GROUP 8      /* query heads per KV head (dk::kMaxGroup) */
+#define DK_TILE_TOKENS 64       /* partition sizes are multiples of this */
+#define DK_REF_PARTITION_SIZE 512 /* the reference's fixed split-K partition */
+
+/*
+ * One decode call.  Shapes (row-major, strides in ELEMENTS, innermost dim
+ * contiguous):
+ *   q, out        [num_seqs, num_q_heads, head_dim]
+ *   k/v cache     [num_blocks, block_size, num_kv_heads, head_dim] with any
+ *                 strides on the first three dims (vLLM interleaved K|V,
+ *                 FlashInfer NHD and HND views are read in place)
+ *   block_tables  int32 [num_seqs, >= ceil(max_seq_len / block_size)], row stride bt_stride
+ *   seq_lens      int32 [num_seqs], read on the device (CUDA-graph safe)
+ * Split-K workspace (fp32, contiguous), used when the plan splits:
+ *   tmp_out       [num_seqs, num_q_heads, max_partitions, head_dim]
+ *   max_logits    [num_seqs, num_q_heads, max_partitions]
+ *   exp_sums      [num_seqs, num_q_heads, max_partitions]
+ * Row (seq * num_q_heads + q_head) * max_partitions + p of the workspace holds
+ * partition p: its normalised partial output, its max scaled logit and its
+ * exp-sum.  Set the three pointers to NULL and max_partitions to 0 when there
+ * is no workspace; the call then runs single-pass.
+ */
+typedef struct DkPagedAttnArgs {
+  void* out;
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  const int32_t* block_tables;
+  const int32_t* seq_lens;
+  float* tmp_out;
+  float* max_logits;
+  float* exp_sums;
+  int64_t q_stride_seq, q_stride_head;
+  int64_t out_stride_seq, out_stride_head;
+  int64_t k_stride_block, k_stride_token, k_stride_head;
+  int64_t v_stride_block, v_stride_token, v_stride_head;
+  int64_t bt_stride;
+  int32_t num_seqs, num_q_heads, num_kv_heads, head_dim, block_size;
+  int32_t num_blocks;     /* size of the caches' first dim; ids outside [0, num_blocks) read zeros on the TMA path */
+  int32_t max_seq_len;    /* host-side upper bound on seq_lens; shapes the grid */
+  int32_t max_partitions; /* workspace capacity (tmp_out.size(2)); 0 = no workspace */
+  int32_t partition_size; /* 0 = planner's choice; else a multiple of 64 tokens */
+  int32_t dtype;          /* DK_DTYPE_* */
+  int32_t flags;          /* DK_FLAG_* */
+  float scale;            /* softmax scale, usually head_dim ** -0.5 */
+} DkPagedAttnArgs;
+
+/* The launch a call would make. */
+typedef struct DkPlan {
+  int32_t path;           /* DK_PATH_* */
+  int32_t partition_size; /* tokens per partition (multiple of 64) */
+  int32_t num_partitions; /* grid partitions; 1 = single pass writing out directly */
+  int32_t split;          /* 1 when partitions go through the workspace and the merge kernel */
+  int32_t num_ctas;       /* partition-kernel CTAs launched (including ones that exit early) */
+  int32_t stages;         /* shared-memory pipeline depth of the TMA path */
+  int32_t smem_bytes;     /* dynamic shared memory of the partition kernel */
+  int32_t launches;       /* kernels launched by one call (1 or 2) */
+} DkPlan;
+
+/*
+ * Paged-attention decode.  Launches on `stream` (asynchronous, no host sync,
+ * no allocation) and returns 0, or a cudaError_t code.  Rejected arguments
+ * return 1 (cudaErrorInvalidValue) without launching.  Capturable in a CUDA
+ * graph: the grid depends only on host-side sizes and max_seq_len.
+ */
+DK_API int dk_paged_attention_decode(const DkPagedAttnArgs* args, dk_stream_t stream);
+
+/* Fill *plan with what dk_paged_attention_decode(args) would launch on the
+ * current device, after the same validation.  Returns 0 or an error code. */
+DK_API int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan);
+
+/*
+ * Workspace partitions to allocate so the planner is never constrained:
+ * ceil(max_seq_len / planned partition size).  num_kv_heads <= 0 means
+ * "unknown" (sizes for the most partitions any num_kv_heads would use).
+ * device < 0 means the current device.  Returns >= 1, or -1 on bad input.
+ */
+DK_API int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                          int32_t max_seq_len, int32_t device);
+
+/* Message describing the calling thread's last failed call ("" if none). */
+DK_API const char* dk_last_error(void);
+
+/*
+ * Bounded device-side waits that gave up since the library loaded on `device`
+ * (every wait on a shared-memory barrier has a ~1 s limit; a kernel that hits
+ * it records the event here and returns instead of hanging).  Synchronous.
+ * Returns 0 and writes the count, or a cudaError_t code.
+ */
+DK_API int dk_device_wait_timeouts(int32_t device, uint32_t* count);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+DK_API int32_t dk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DK_PAGED_ATTENTION_H_ */

@@ -1,0 +1,158 @@
+"""CPU: the C ABI library loads, exports every entry point the header
+declares, validates arguments like the reference, and plans launches -- all
+without a GPU (no compute calls)."""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from decodekernels_b200 import capi
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "dk_paged_attention.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"DK_API\s+[\w\s\*]+?\b(dk_\w+)\s*\(", text)
+
+
+def test_header_declares_the_bound_entry_points():
+    assert set(_declared()) == set(capi.EXPORTED)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = capi.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (dk_\w+)", out))
+    assert set(_declared()) <= exported
+    assert capi.version() == 100
+
+
+def test_struct_layout_matches_header():
+    # 9 pointers + 11 int64 + 11 int32 + 1 float = 208 bytes, no padding surprises
+    assert ctypes.sizeof(capi.DkPagedAttnArgs) == 208
+    assert ctypes.sizeof(capi.DkPlan) == 32
+
+
+def _args(**over):
+    """CPU tensors only provide shapes/strides/pointers; nothing is launched."""
+    n, hq, hkv, d, bs = over.pop("n", 4), over.pop("hq", 32), over.pop("hkv", 8), over.pop("d", 128), over.pop("bs", 16)
+    dtype = over.pop("dtype", torch.bfloat16)
+    q = torch.zeros(n, hq, d, dtype=dtype)
+    k = torch.zeros(64, bs, hkv, d, dtype=dtype)
+    bt = torch.zeros(max(n, 1), 64, dtype=torch.int32)
+    sl = torch.zeros(max(n, 1), dtype=torch.int32)
+    out = torch.zeros_like(q)
+    max_seq_len = over.pop("max_seq_len", 513)
+    ws = over.pop("ws", None)
+    a = capi.make_args(q, k, k, bt, sl, d**-0.5, max_seq_len, out, ws, over.pop("partition_size", 0),
+                       over.pop("force_simt", False))
+    for key, val in over.items():
+        setattr(a, key, val)
+    return a
+
+
+def _plan(a):
+    p = capi.DkPlan()
+    rc = capi.load().dk_plan(ctypes.byref(a), ctypes.byref(p))
+    return rc, p.as_dict()
+
+
+@pytest.mark.parametrize(
+    "override,msg",
+    [
+        (dict(hq=128, hkv=8), "GQA group"),
+        (dict(d=96), "head_dim"),
+        (dict(hq=12, hkv=8), "multiple of num_kv_heads"),
+        (dict(max_seq_len=-1), "max_seq_len"),
+        (dict(dtype_code=7), "float16 or bfloat16"),
+        (dict(k_stride_token=130), "multiples of head_dim / 32"),
+        (dict(partition_size=100), "partition_size"),
+        (dict(num_seqs=70000), "num_seqs"),
+    ],
+)
+def test_validation_rejects_like_reference(override, msg):
+    if "dtype_code" in override:
+        a = _args()
+        a.dtype = override["dtype_code"]
+    else:
+        a = _args(**override)
+    rc, _ = _plan(a)
+    assert rc == 1  # cudaErrorInvalidValue
+    assert msg in capi.last_error()
+    # the launch entry point rejects the same way, before touching the GPU
+    assert capi.load().dk_paged_attention_decode(ctypes.byref(a), None) == 1
+
+
+def test_misaligned_pointer_is_rejected():
+    a = _args()
+    a.k_cache += 2  # not aligned to head_dim / 16 = 8 bytes
+    rc, _ = _plan(a)
+    assert rc == 1 and "aligned" in capi.last_error()
+
+
+def test_plan_without_workspace_is_single_pass():
+    rc, p = _plan(_args(max_seq_len=4000))
+    assert rc == 0
+    assert p["split"] == 0 and p["num_partitions"] == 1 and p["partition_size"] == 4032
+    assert p["path"] == capi.DK_PATH_TMA_MMA and p["launches"] == 1
+
+
+def _ws(n, hq, parts, d=128):
+    return (torch.zeros(n, hq, parts, d), torch.zeros(n, hq, parts), torch.zeros(n, hq, parts))
+
+
+def test_plan_splits_to_fill_the_gpu():
+    # batch 1, 128K context, 8 KV heads: partitions of at most 512 tokens
+    parts = capi.num_partitions(1, 8, 128, 16, 131072)
+    rc, p = _plan(_args(n=1, hq=64, hkv=8, max_seq_len=131072, ws=_ws(1, 64, parts)))
+    assert rc == 0 and p["split"] == 1 and p["launches"] == 2
+    assert p["partition_size"] <= 512 and p["partition_size"] % 64 == 0
+    assert p["num_partitions"] * p["partition_size"] >= 131072
+    assert p["num_ctas"] == p["num_partitions"] * 8
+
+
+def test_plan_respects_a_small_workspace():
+    # the reference's own sizing: ceil(L / 512) partitions -> partitions of 512
+    rc, p = _plan(_args(n=1, hq=64, hkv=8, max_seq_len=131072, ws=_ws(1, 64, 256)))
+    assert rc == 0 and p["num_partitions"] <= 256 and p["partition_size"] == 512
+    rc, p = _plan(_args(n=1, hq=64, hkv=8, max_seq_len=131072, ws=_ws(1, 64, 10)))
+    assert rc == 0 and p["num_partitions"] <= 10 and p["partition_size"] % 64 == 0
+
+
+def test_plan_fixed_partition_size():
+    rc, p = _plan(_args(max_seq_len=3000, ws=_ws(4, 32, 47), partition_size=64))
+    assert rc == 0 and p["partition_size"] == 64 and p["num_partitions"] == 47
+
+
+def test_plan_path_choice():
+    assert _plan(_args(bs=16))[1]["path"] == capi.DK_PATH_TMA_MMA
+    assert _plan(_args(bs=256))[1]["path"] == capi.DK_PATH_TMA_MMA
+    assert _plan(_args(bs=8))[1]["path"] == capi.DK_PATH_TMA_MMA
+    assert _plan(_args(bs=4))[1]["path"] == capi.DK_PATH_SIMT
+    assert _plan(_args(bs=48))[1]["path"] == capi.DK_PATH_SIMT
+    assert _plan(_args(force_simt=True))[1]["path"] == capi.DK_PATH_SIMT
+
+
+def test_num_partitions_covers_reference_sizing():
+    for n, hkv, L in [(1, 8, 131072), (64, 8, 4096), (256, 8, 32768), (4, 8, 513), (128, 1, 32768)]:
+        p = capi.num_partitions(n, hkv, 128, 16, L)
+        assert p >= -(-L // 512)
+        assert capi.num_partitions(n, 0, 128, 16, L) >= p  # unknown head count sizes for the most
+    assert capi.num_partitions(4, 8, 128, 16, 0) == 1
+    with pytest.raises(ValueError):
+        capi.num_partitions(4, 8, 96, 16, 100)
+
+
+def test_empty_batch_is_a_no_op():
+    a = _args(n=0)
+    rc, p = _plan(a)
+    assert rc == 0 and p["path"] == capi.DK_PATH_NONE
+    assert capi.load().dk_paged_attention_decode(ctypes.byref(a), None) == 0
