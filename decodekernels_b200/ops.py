@@ -91,7 +91,11 @@ def alloc_workspace(num_seqs: int, num_q_heads: int, head_dim: int, max_seq_len:
     count (at least the reference's ``ceil(max_seq_len / 512)``).
     """
     _require()
-    parts = capi.num_partitions(num_seqs, num_kv_heads or 0, head_dim, block_size, max_seq_len, _device_index(device))
+    try:
+        parts = capi.num_partitions(num_seqs, num_kv_heads or 0, head_dim, block_size, max_seq_len,
+                                    _device_index(device))
+    except ValueError:
+        parts = 1  # unsupported shape: size like the reference and let the op report the error
     parts = max(parts, num_partitions(max_seq_len))
     if parts <= 1 and max_seq_len <= PARTITION_SIZE:
         empty = torch.empty(0, dtype=torch.float32, device=device)
