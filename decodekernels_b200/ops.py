@@ -44,7 +44,7 @@ try:
     capi.load()
     _AVAILABLE = True
     _IMPORT_ERROR: Exception | None = None
-except (ImportError, OSError, RuntimeError) as e:  # native library not built
+except Exception as e:  # native library missing or stale: every op raises, nothing falls back
     _AVAILABLE = False
     _IMPORT_ERROR = e
 
