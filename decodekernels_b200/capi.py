@@ -26,8 +26,10 @@ DK_MAX_GQA_GROUP = 8
 DK_TILE_TOKENS = 64
 DK_REF_PARTITION_SIZE = 512
 
+DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
+
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
-            "dk_device_wait_timeouts", "dk_version")
+            "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -98,6 +100,8 @@ def load() -> ctypes.CDLL:
         lib = ctypes.CDLL(str(LIB_PATH))
         lib.dk_paged_attention_decode.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.c_void_p]
         lib.dk_paged_attention_decode.restype = ctypes.c_int
+        lib.dk_paged_attention_decode_noalloc.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.c_void_p]
+        lib.dk_paged_attention_decode_noalloc.restype = ctypes.c_int
         lib.dk_plan.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.POINTER(DkPlan)]
         lib.dk_plan.restype = ctypes.c_int
         lib.dk_num_partitions.argtypes = [ctypes.c_int32] * 6
@@ -202,4 +206,23 @@ def decode(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out,
     rc = load().dk_paged_attention_decode(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_paged_attention_decode failed ({rc}): {last_error()}")
+    return rc
+
+
+def decode_noalloc(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, stream=None) -> int:
+    """dk_paged_attention_decode_noalloc: the decode for callers that cannot
+    allocate device memory (plugin hosts and runtimes that own all memory
+    besides a kernel's inputs and outputs, FFI hosts without a CUDA
+    allocator).  Split-K partials go to the library's static scratch of
+    DK_NOALLOC_SCRATCH_BYTES; calls that would need more are rejected
+    (RuntimeError).  Calls that overlap on the GPU share that scratch and race.
+    """
+    import torch
+
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, None)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
+    rc = load().dk_paged_attention_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_paged_attention_decode_noalloc failed ({rc}): {last_error()}")
     return rc

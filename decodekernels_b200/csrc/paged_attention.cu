@@ -440,6 +440,33 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   }
 }
 
+// ---------------------------------------------------------------------------
+// Scratch for dk_paged_attention_decode_noalloc: the split-K partials of
+// callers that cannot allocate.  File-scope, so every GPU that loads this
+// library holds it until the process exits.  Host code must not pass the
+// symbol itself to a kernel (on the host it is only a stand-in); the device
+// address comes from cudaGetSymbolAddress, once per device.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float g_noalloc_scratch[DK_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch on `dev` (the current device), looked up on
+// the first call for that device.
+int noalloc_scratch(int dev, float** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(1, "device %d out of range for the no-allocation scratch", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return fail_cuda(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
 }  // namespace
 }  // namespace dkb
 
@@ -459,6 +486,41 @@ int dk_paged_attention_decode(const DkPagedAttnArgs* args, dk_stream_t stream) {
   if (pl.split && args->max_partitions < pl.num_partitions)
     return dkb::fail(1, "split-K workspace too small: %d partitions needed", pl.num_partitions);
   return dkb::launch(*args, pl, dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate(args)) return e;
+  if (args->max_partitions != 0 || args->tmp_out || args->max_logits || args->exp_sums)
+    return dkb::fail(1, "dk_paged_attention_decode_noalloc takes no workspace: set max_partitions to 0 and the "
+                        "workspace pointers to NULL");
+  if (args->num_seqs == 0) return 0;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  // Plan as if the caller had allocated the planner's full workspace, so the
+  // partitioning (and the result) is the same as dk_paged_attention_decode's.
+  DkPagedAttnArgs a = *args;
+  a.max_partitions = INT_MAX;
+  DkPlan pl;
+  dkb::make_plan(a, dev, &pl);
+  a.max_partitions = 0;
+  if (pl.split) {
+    const size_t rows = static_cast<size_t>(a.num_seqs) * a.num_q_heads * pl.num_partitions;
+    const size_t need = rows * (static_cast<size_t>(a.head_dim) + 2) * sizeof(float);
+    if (need > DK_NOALLOC_SCRATCH_BYTES)
+      return dkb::fail(1,
+                       "dk_paged_attention_decode_noalloc: this call needs %zu bytes of split-K scratch "
+                       "(%d sequences x %d query heads x %d partitions x (head_dim + 2) floats) but the static "
+                       "scratch holds %u bytes; call dk_paged_attention_decode with a caller-allocated workspace",
+                       need, a.num_seqs, a.num_q_heads, pl.num_partitions, DK_NOALLOC_SCRATCH_BYTES);
+    float* base = nullptr;
+    if (int e = dkb::noalloc_scratch(dev, &base)) return e;
+    a.tmp_out = base;
+    a.max_logits = base + rows * a.head_dim;
+    a.exp_sums = a.max_logits + rows;
+    a.max_partitions = pl.num_partitions;
+  }
+  return dkb::launch(a, pl, dev, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan) {

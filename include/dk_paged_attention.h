@@ -126,6 +126,29 @@ typedef struct DkPlan {
  */
 DK_API int dk_paged_attention_decode(const DkPagedAttnArgs* args, dk_stream_t stream);
 
+/*
+ * Same decode as dk_paged_attention_decode, for callers that cannot allocate
+ * device memory: no counterpart in the reference (whose wrapper always
+ * allocated the split-K workspace with torch).  Examples are inference
+ * runtimes and plugin hosts that hand a kernel only its inputs and outputs
+ * and own every other byte of device memory, and host languages whose FFI has
+ * no CUDA allocator.  Pass args with no workspace (max_partitions 0, the three
+ * workspace pointers NULL); when the plan splits, the partials go to a
+ * library-owned scratch array of DK_NOALLOC_SCRATCH_BYTES in device memory
+ * that every GPU using this library holds until the process exits.  Calls
+ * whose plan needs more scratch than that (num_seqs * num_q_heads *
+ * partitions * (head_dim + 2) * 4 bytes) are rejected with status 1 and a
+ * message; use dk_paged_attention_decode with your own workspace for them.
+ * Nothing here calls cudaMalloc / cudaFree or any allocating routine.
+ * The first call on each device looks up the scratch's device address (with
+ * that device current); make that first call before any stream capture.
+ * All calls share the one array: calls that can overlap on the GPU (other
+ * streams, other threads) race on it.  Nothing in it needs to start at zero:
+ * each call writes every scratch row it reads.
+ */
+#define DK_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+DK_API int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t stream);
+
 /* Fill *plan with what dk_paged_attention_decode(args) would launch on the
  * current device, after the same validation.  Returns 0 or an error code. */
 DK_API int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan);
