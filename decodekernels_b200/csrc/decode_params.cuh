@@ -5,10 +5,8 @@
 
 namespace dkb {
 
-constexpr int kTileTokens = 64;      // tokens per pipeline stage (one CTA-wide tile)
+constexpr int kTileTokens = 64;      // partition-size granularity; every pipeline tile divides it
 constexpr int kSubTokens = 16;       // tokens per consumer warp per tile (mma M)
-constexpr int kConsumerWarps = 4;    // kTileTokens / kSubTokens
-constexpr int kTmaThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
 constexpr int kSimtThreads = 128;
 constexpr int kMergeThreads = 256;
 constexpr int kMaxGroup = 8;         // query heads per KV head (mma N)
@@ -37,12 +35,13 @@ struct DecodeParams {
   int group;           // num_q_heads / num_kv_heads
   int block_size;
   int num_blocks;      // cache blocks; ids outside [0, num_blocks) read as zeros
-  int rows_per_op;     // token rows per TMA box: min(block_size, kTileTokens)
+  int bs_log2;         // log2(block_size) (TMA path: power-of-two block sizes)
+  int rows_log2;       // log2 of token rows per TMA box: min(block_size, tile)
   int partition_size;  // tokens per partition, a multiple of kTileTokens
   int num_partitions;  // partitions in the grid
   int ws_partitions;   // workspace row stride (capacity)
   int split;           // 1: partitions write the workspace and the merge kernel writes out
-  int slot_head, slot_tok, slot_blk;  // tensor-map coordinate slot (1..3) of each cache dim
+  int kv_fused;        // 1: one tensor map covers K and V (vLLM's interleaved K|V rows)
   float scale_log2;    // softmax scale * log2(e)
 };
 

@@ -110,6 +110,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// 5-D tiled load of one box into CTA-local shared memory, completing on `bar`.
+// (No multicast: the destination is this CTA's own shared memory.)
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) writes to the same bytes.
 __device__ __forceinline__ void fence_proxy_async_smem() {

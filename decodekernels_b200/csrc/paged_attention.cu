@@ -28,9 +28,21 @@ namespace dkb {
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
-constexpr int kMinPartition = 128;
-constexpr int kMaxPartition = 512;
-constexpr int kWaves = 4;  // planner target: ~4 resident waves of partition CTAs
+// Planner: partitions are sized so that the grid is about one wave of
+// kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
+// [kMinPartition, kMaxPartition] tokens (overridable for tuning sweeps).
+#ifndef DK_PLAN_CTAS_PER_SM
+#define DK_PLAN_CTAS_PER_SM 2
+#endif
+#ifndef DK_PLAN_MIN_PARTITION
+#define DK_PLAN_MIN_PARTITION 128
+#endif
+#ifndef DK_PLAN_MAX_PARTITION
+#define DK_PLAN_MAX_PARTITION 4096
+#endif
+constexpr int kPlanCtasPerSm = DK_PLAN_CTAS_PER_SM;
+constexpr int kMinPartition = DK_PLAN_MIN_PARTITION;
+constexpr int kMaxPartition = DK_PLAN_MAX_PARTITION;
 
 thread_local char g_last_error[512] = {0};
 
@@ -49,20 +61,51 @@ int fail_cuda(cudaError_t e, const char* what) {
 constexpr int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 constexpr int round_up(long long a, long long b) { return static_cast<int>(((a + b - 1) / b) * b); }
 
+// Pipeline depth and consumer warps per head_dim (overridable at build time
+// for tuning sweeps).  Two stages with several CTAs per SM beat deeper rings
+// with fewer CTAs: the stream of each CTA has a serial per-tile cost, so
+// bandwidth comes from concurrent CTAs.
+#ifndef DK_TMA_STAGES_D64
+#define DK_TMA_STAGES_D64 2
+#endif
+#ifndef DK_TMA_STAGES_D128
+#define DK_TMA_STAGES_D128 2
+#endif
+#ifndef DK_TMA_STAGES_D256
+#define DK_TMA_STAGES_D256 2
+#endif
+#ifndef DK_TMA_WARPS_D64
+#define DK_TMA_WARPS_D64 4
+#endif
+#ifndef DK_TMA_WARPS_D128
+#define DK_TMA_WARPS_D128 4
+#endif
+#ifndef DK_TMA_WARPS_D256
+#define DK_TMA_WARPS_D256 2
+#endif
+
+template <int D>
+struct TmaShape {
+  static constexpr int kStages = D == 64 ? DK_TMA_STAGES_D64 : (D == 128 ? DK_TMA_STAGES_D128 : DK_TMA_STAGES_D256);
+  static constexpr int kWarps = D == 64 ? DK_TMA_WARPS_D64 : (D == 128 ? DK_TMA_WARPS_D128 : DK_TMA_WARPS_D256);
+  using Cfg = TmaConfig<D, kStages, kWarps>;
+};
+
 template <int D>
 constexpr int tma_stages() {
-  return D == 64 ? 4 : 3;
+  return TmaShape<D>::kStages;
 }
 
-// Resident partition CTAs per SM on the TMA path (shared memory bound).
-int tma_ctas_per_sm(int D) { return D == 64 ? 3 : (D == 128 ? 2 : 1); }
+int tma_tile(int D) {
+  return D == 64 ? TmaShape<64>::Cfg::kTile : (D == 128 ? TmaShape<128>::Cfg::kTile : TmaShape<256>::Cfg::kTile);
+}
 
 int smem_for(int path, int D) {
   if (path == DK_PATH_TMA_MMA) {
     switch (D) {
-      case 64: return TmaConfig<64, tma_stages<64>()>::kSmemBytes;
-      case 128: return TmaConfig<128, tma_stages<128>()>::kSmemBytes;
-      default: return TmaConfig<256, tma_stages<256>()>::kSmemBytes;
+      case 64: return TmaShape<64>::Cfg::kSmemBytes;
+      case 128: return TmaShape<128>::Cfg::kSmemBytes;
+      default: return TmaShape<256>::Cfg::kSmemBytes;
     }
   }
   switch (D) {
@@ -147,23 +190,39 @@ int validate(const DkPagedAttnArgs* a) {
 // ---------------------------------------------------------------------------
 // Planner
 // ---------------------------------------------------------------------------
-// Tokens per partition before workspace constraints: split until the grid
-// holds ~kWaves waves of resident CTAs, in partitions of 128..512 tokens.
+// Tokens per partition before workspace constraints.  The host knows only
+// max_seq_len, so:
+// * one sequence (lengths cannot vary): spread its work over ~one wave of
+//   kPlanCtasPerSm CTAs per SM;
+// * several sequences with fewer (sequence, kv_head) pairs than ~4 waves of
+//   CTAs: lengths may vary, so keep partitions <= kVariedPartition tokens
+//   for balance;
+// * many pairs: partitions up to kMaxPartition (plenty of CTAs already).
+// Always a multiple of 64 tokens within [kMinPartition, kMaxPartition].
+#ifndef DK_PLAN_VARIED_PARTITION
+#define DK_PLAN_VARIED_PARTITION 1024
+#endif
+constexpr int kVariedPartition = DK_PLAN_VARIED_PARTITION;
+
 int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms) {
+  (void)head_dim;
   const long long pairs = std::max<long long>(1, static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1));
-  const long long target = static_cast<long long>(kWaves) * sms * tma_ctas_per_sm(head_dim);
-  const long long want = std::max<long long>(1, (target + pairs - 1) / pairs);
-  int ps = round_up(ceil_div(max_seq_len, want), DK_TILE_TOKENS);
-  return std::min(std::max(ps, kMinPartition), kMaxPartition);
+  const long long slots = static_cast<long long>(kPlanCtasPerSm) * sms;
+  const long long work = pairs * std::max(max_seq_len, 1);
+  int ps = round_up((work + slots - 1) / slots, DK_TILE_TOKENS);
+  int cap = kMaxPartition;
+  if (num_seqs > 1 && pairs < 4 * slots) cap = std::min(cap, kVariedPartition);
+  return std::min(std::max(ps, kMinPartition), cap);
 }
 
 // Path choice: the TMA path needs 16-byte aligned bases and strides (the
-// tensor-map rules) and a block size that tiles the 64-token stage.
+// tensor-map rules) and a power-of-two block size of at least 8 tokens (so a
+// 64-token tile is whole pages, or a 64-row slice of one page, and the
+// 128-byte swizzle spans 8 rows of a page).
 bool tma_eligible(const DkPagedAttnArgs& a) {
   if (a.flags & DK_FLAG_FORCE_SIMT) return false;
   const int bs = a.block_size;
-  if (bs < 8) return false;
-  if (!((bs <= DK_TILE_TOKENS && DK_TILE_TOKENS % bs == 0) || bs % DK_TILE_TOKENS == 0)) return false;
+  if (bs < 8 || (bs & (bs - 1)) != 0) return false;
   if (!aligned(a.k_cache, 16) || !aligned(a.v_cache, 16)) return false;
   const int64_t sizes[3] = {a.num_blocks, a.block_size, a.num_kv_heads};
   const int64_t ks[3] = {a.k_stride_block, a.k_stride_token, a.k_stride_head};
@@ -174,6 +233,20 @@ bool tma_eligible(const DkPagedAttnArgs& a) {
     if (ks[i] * 2 >= (int64_t(1) << 40) || vs[i] * 2 >= (int64_t(1) << 40)) return false;
   }
   return true;
+}
+
+// K and V are the two halves of one row (vLLM's [blocks, heads, bs, 2*D]
+// buffer viewed as two [blocks, bs, heads, D] tensors): one map covers both.
+bool kv_fused(const DkPagedAttnArgs& a) {
+  return static_cast<const char*>(a.v_cache) == static_cast<const char*>(a.k_cache) + a.head_dim * 2 &&
+         a.k_stride_block == a.v_stride_block && a.k_stride_token == a.v_stride_token &&
+         a.k_stride_head == a.v_stride_head;
+}
+
+int ilog2(int x) {
+  int r = 0;
+  while ((1 << (r + 1)) <= x) ++r;
+  return r;
 }
 
 void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
@@ -204,7 +277,9 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   pl->num_partitions = parts;
   pl->split = parts > 1 ? 1 : 0;
   pl->num_ctas = static_cast<int32_t>(std::min<long long>(INT_MAX, 1LL * parts * a.num_kv_heads * a.num_seqs));
-  pl->stages = pl->path == DK_PATH_TMA_MMA ? (a.head_dim == 64 ? 4 : 3) : 0;
+  pl->stages = pl->path == DK_PATH_TMA_MMA
+                   ? (a.head_dim == 64 ? tma_stages<64>() : (a.head_dim == 128 ? tma_stages<128>() : tma_stages<256>()))
+                   : 0;
   pl->smem_bytes = smem_for(pl->path, a.head_dim);
   pl->launches = pl->split ? 2 : 1;
 }
@@ -237,7 +312,7 @@ struct MapKey {
   int64_t strides[3];
   int64_t sizes[3];
   int rows;
-  int head_dim;
+  int col_blocks;
   int dev;
   bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
@@ -245,7 +320,6 @@ struct MapKey {
 struct MapEntry {
   MapKey key;
   CUtensorMap map;
-  int slot_head, slot_tok, slot_blk;
   bool used;
 };
 
@@ -254,13 +328,13 @@ std::mutex g_map_mu;
 MapEntry g_maps[kMapCache];
 int g_map_next = 0;
 
-// 4-D map over one cache view: dim 0 = head_dim (contiguous), dims 1..3 =
-// {head, token, block} ordered by increasing stride.  The box is one
-// 64-column half of `rows` token rows of one head of one page, 128-byte
-// swizzled.  Writes each dim's coordinate slot.
+// 5-D map over one cache view (or over K and V together when interleaved):
+// dims (64 columns, token, 64-column block, head, block) with strides
+// (2 B, token stride, 128 B, head stride, block stride).  The box is all
+// `col_blocks` column blocks of `rows` token rows of one head of one page and
+// lands in shared memory as [column block][row][128 B], 128-byte swizzled.
 int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, int64_t num_blocks, int block_size,
-              int num_kv_heads, int head_dim, int rows, int dev, CUtensorMap* out, int* slot_head, int* slot_tok,
-              int* slot_blk) {
+              int num_kv_heads, int col_blocks, int rows, int dev, CUtensorMap* out) {
   MapKey key;
   std::memset(&key, 0, sizeof(key));
   key.ptr = ptr;
@@ -271,62 +345,41 @@ int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, i
   key.sizes[1] = block_size;
   key.sizes[2] = num_blocks;
   key.rows = rows;
-  key.head_dim = head_dim;
+  key.col_blocks = col_blocks;
   key.dev = dev;
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
     for (auto& e : g_maps) {
       if (e.used && e.key == key) {
         *out = e.map;
-        *slot_head = e.slot_head;
-        *slot_tok = e.slot_tok;
-        *slot_blk = e.slot_blk;
         return 0;
       }
     }
   }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(static_cast<int>(cudaErrorNotSupported), "cuTensorMapEncodeTiled is unavailable");
-
-  // dims 0..2 of the sort: 0 = head, 1 = token, 2 = block
-  int64_t size[3] = {num_kv_heads, block_size, num_blocks};
-  int64_t stride[3] = {s_head, s_tok, s_block};
-  for (int i = 0; i < 3; ++i) {
-    if (size[i] <= 1) stride[i] = 16 / 2;  // never stepped; any legal stride will do
-  }
-  int order[3] = {0, 1, 2};
-  std::sort(order, order + 3, [&](int x, int y) { return stride[x] != stride[y] ? stride[x] < stride[y] : x < y; });
-  cuuint64_t gdim[4];
-  cuuint64_t gstride[3];
-  cuuint32_t box[4];
-  cuuint32_t estride[4] = {1, 1, 1, 1};
-  gdim[0] = static_cast<cuuint64_t>(head_dim);
-  box[0] = 64;
-  int slots[3] = {0, 0, 0};
-  for (int k = 0; k < 3; ++k) {
-    const int which = order[k];
-    gdim[k + 1] = static_cast<cuuint64_t>(size[which]);
-    gstride[k] = static_cast<cuuint64_t>(stride[which]) * 2;
-    box[k + 1] = which == 1 ? static_cast<cuuint32_t>(rows) : 1u;
-    slots[which] = k + 1;
-  }
+  // a dimension of size 1 is never stepped: any legal stride will do
+  auto legal = [](int64_t size, int64_t stride_elems) -> cuuint64_t {
+    const int64_t b = stride_elems * 2;
+    return static_cast<cuuint64_t>(size <= 1 || b <= 0 || b % 16 != 0 ? 16 : b);
+  };
+  const cuuint64_t gdim[5] = {64, static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(col_blocks),
+                              static_cast<cuuint64_t>(num_kv_heads), static_cast<cuuint64_t>(num_blocks)};
+  const cuuint64_t gstride[4] = {legal(block_size, s_tok), 128, legal(num_kv_heads, s_head),
+                                 legal(num_blocks, s_block)};
+  const cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows), static_cast<cuuint32_t>(col_blocks), 1, 1};
+  const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
-  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(ptr), gdim, gstride, box, estride,
+  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5, const_cast<void*>(ptr), gdim, gstride, box, estride,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(1, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   *out = map;
-  *slot_head = slots[0];
-  *slot_tok = slots[1];
-  *slot_blk = slots[2];
   std::lock_guard<std::mutex> lk(g_map_mu);
   MapEntry& e = g_maps[g_map_next];
   g_map_next = (g_map_next + 1) % kMapCache;
   e.key = key;
   e.map = map;
-  e.slot_head = slots[0];
-  e.slot_tok = slots[1];
-  e.slot_blk = slots[2];
   e.used = true;
   return 0;
 }
@@ -355,31 +408,25 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
                   static_cast<unsigned>(a.num_seqs));
   cudaError_t e;
   if (pl.path == DK_PATH_TMA_MMA) {
-    constexpr int S = tma_stages<D>();
+    using Shape = TmaShape<D>;
     static bool attr_done[kMaxDevices] = {false};
-    auto kernel = paged_decode_tma_kernel<T, D, S>;
-    const int smem = TmaConfig<D, S>::kSmemBytes;
+    auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps>;
+    const int smem = Shape::Cfg::kSmemBytes;
     e = ensure_smem_attr(kernel, smem, dev, attr_done);
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(partition kernel)");
     CUtensorMap kmap, vmap;
-    int sh, st, sb, sh2, st2, sb2;
+    const int rows = 1 << p.rows_log2;
+    p.kv_fused = kv_fused(a) ? 1 : 0;
     if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
-                          a.num_kv_heads, D, p.rows_per_op, dev, &kmap, &sh, &st, &sb))
+                          a.num_kv_heads, (p.kv_fused ? 2 : 1) * (D / 64), rows, dev, &kmap))
       return r;
-    if (int r = build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks, a.block_size,
-                          a.num_kv_heads, D, p.rows_per_op, dev, &vmap, &sh2, &st2, &sb2))
+    if (p.kv_fused) {
+      vmap = kmap;  // unused
+    } else if (int r = build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks,
+                                 a.block_size, a.num_kv_heads, D / 64, rows, dev, &vmap)) {
       return r;
-    if (sh != sh2 || st != st2 || sb != sb2) {
-      // K and V views order their dims differently: fall back to the CUDA-core kernel.
-      DkPlan simt = pl;
-      simt.path = DK_PATH_SIMT;
-      simt.smem_bytes = SimtConfig<D>::kSmemBytes;
-      return launch_typed<T, D>(a, simt, p, dev, stream);
     }
-    p.slot_head = sh;
-    p.slot_tok = st;
-    p.slot_blk = sb;
-    e = launch_pdl(kernel, grid, dim3(kTmaThreads), smem, stream, kmap, vmap, p);
+    e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
     if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch");
   } else {
     auto kernel = paged_decode_simt_kernel<T, D>;
@@ -421,7 +468,8 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.group = a.num_q_heads / a.num_kv_heads;
   p.block_size = a.block_size;
   p.num_blocks = a.num_blocks;
-  p.rows_per_op = std::min(a.block_size, DK_TILE_TOKENS);
+  p.bs_log2 = ilog2(a.block_size);
+  p.rows_log2 = std::min(p.bs_log2, ilog2(tma_tile(a.head_dim)));
   p.partition_size = pl.partition_size;
   p.num_partitions = pl.num_partitions;
   p.ws_partitions = pl.split ? a.max_partitions : 1;
