@@ -310,6 +310,26 @@ def run_gpu_arm(args) -> None:
     if sampler:
         sampler.stop()
 
+    # With N GPUs, also time the variant whose consumer needs every head on
+    # every rank: decode + NCCL all-gather of the per-head outputs.
+    gather_s = None
+    if world > 1:
+        from decodekernels_b200.sharded import gather_heads, head_shard
+
+        shard = head_shard(batch.config.num_q_heads, batch.config.num_kv_heads, rank, world)
+        for _ in range(3):
+            gather_heads(out, shard)
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record(stream)
+        for _ in range(args.steps):
+            step()
+            gather_heads(out, shard)
+        ge.record(stream)
+        torch.cuda.synchronize()
+        gather_s = gs.elapsed_time(ge) * 1e-3
+
     # End to end through the public API with pinned host buffers: H2D of q,
     # block tables and lengths, the call, D2H of the output, every step.
     h_q = q.cpu().pin_memory()
@@ -354,15 +374,16 @@ def run_gpu_arm(args) -> None:
 
     kv_local = batch.kv_bytes()
     alg_local = batch.algorithmic_bytes()
-    stats = torch.tensor([device_s, e2e_s, float(kv_local), float(alg_local)], dtype=torch.float64, device=dev)
+    stats = torch.tensor([device_s, e2e_s, gather_s or 0.0, float(kv_local), float(alg_local)], dtype=torch.float64,
+                         device=dev)
     if world > 1:
         import torch.distributed as dist
 
-        tmax = stats[:2].clone()
+        tmax = stats[:3].clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        sums = stats[2:].clone()
+        sums = stats[3:].clone()
         dist.all_reduce(sums, op=dist.ReduceOp.SUM)
-        device_s, e2e_s = tmax.tolist()
+        device_s, e2e_s, gather_s = tmax.tolist()
         kv_total, alg_total = sums.tolist()
     else:
         kv_total, alg_total = float(kv_local), float(alg_local)
@@ -401,6 +422,9 @@ def run_gpu_arm(args) -> None:
             "e2e": {"value": kv_total / (e2e_s / e_steps) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e_steps, "api": "decodekernels_b200.paged_attention_decode"},
             "gpu_launches": args.steps * plan["launches"],
+            "with_gather": None if not gather_s else {
+                "us_per_call": gather_s / args.steps * 1e6, "value": kv_total / (gather_s / args.steps) / 1e12,
+                "unit": UNIT, "note": "decode + NCCL all-gather of the per-head outputs to every rank"},
             "clocks": sampler.summary(t0, t1) if sampler else None,
             "wall_s_timed": t1 - t0,
         }

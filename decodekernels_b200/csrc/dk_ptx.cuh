@@ -99,17 +99,6 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
-// 4-D tiled load of one box into CTA-local shared memory, completing on `bar`.
-// (No multicast: the destination is this CTA's own shared memory.)
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
-                                            uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
 // 5-D tiled load of one box into CTA-local shared memory, completing on `bar`.
 // (No multicast: the destination is this CTA's own shared memory.)
 __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3, int c4,
