@@ -276,8 +276,10 @@ def run_gpu_arm(args) -> None:
     torch.cuda.synchronize()
     parity = _check_parity(batch, out, rank)
 
+    # Inputs several times the 126 MB L2 (c2-c5) stream through it with no
+    # reuse between steps; smaller ones (c1) get a 256 MB write between steps.
     l2_bytes = 126 * 1024 * 1024
-    flush = batch.kv_bytes() < 4 * l2_bytes
+    flush = batch.kv_bytes() < 3 * l2_bytes
     flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.int32, device=dev) if flush else None
 
     sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None

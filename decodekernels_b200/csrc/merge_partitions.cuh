@@ -2,14 +2,17 @@
 // paged_attention_reduce_kernel, csrc/paged_attention.cuh:227-269):
 //   M = max_i m_i,  w_i = s_i exp(m_i - M),  out = sum_i w_i o_i / sum_i w_i
 // over the live partitions num_parts = min(ceil(L / partition_size), P);
-// zeros when L <= 0.
+// zeros when L <= 0.  Sequences with a single live partition were already
+// written to `out` by the partition kernel and are skipped here.
 //
-// One CTA of 8 warps per (q_head, seq).  Warp w folds partitions w, w+8, ...
-// with each lane holding head_dim / 32 consecutive floats of the partial
-// output (one 8/16/32-byte load per partition, unrolled so several
-// partitions are in flight), then the warps are summed through shared memory.
-// Launched with programmatic dependent launch: the CTAs start while the
-// partition kernel drains and wait for its results in griddepcontrol.wait.
+// One CTA of 4 warps per (query head, sequence).  Every warp finds the max
+// over all live partitions by itself (lane-strided loads + shuffles), then
+// folds the partitions w, w+4, ... with each lane holding head_dim / 32
+// consecutive floats of a partial output (one 8/16/32-byte load per
+// partition, unrolled so several are in flight); one barrier joins the four
+// partial sums.  Launched with programmatic dependent launch: the CTAs start
+// while the partition kernel drains and wait for its results in
+// griddepcontrol.wait.
 #pragma once
 
 #include "decode_params.cuh"
@@ -22,15 +25,14 @@ struct alignas(4 * N) F32Vec {
   float v[N];
 };
 
+constexpr int kMergeWarps = kMergeThreads / 32;
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const DecodeParams p) {
-  constexpr int WARPS = kMergeThreads / 32;
   constexpr int V = D / 32;
   using Vec = F32Vec<V>;
-  __shared__ float red[WARPS][D];
-  __shared__ float wsum[WARPS];
-  __shared__ float wmax[WARPS];
-
+  __shared__ float red[kMergeWarps][D];
+  __shared__ float wsums[kMergeWarps];
   const int q_head = blockIdx.x;
   const int seq = blockIdx.y;
   const int warp = threadIdx.x >> 5;
@@ -44,45 +46,42 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
     return;
   }
   const int num_parts = min((seq_len + p.partition_size - 1) / p.partition_size, p.num_partitions);
+  if (num_parts <= 1) return;  // written by the partition kernel
+
   const int64_t row0 = (static_cast<int64_t>(seq) * p.num_q_heads + q_head) * p.ws_partitions;
   const float* ml = p.max_logits + row0;
   const float* es = p.exp_sums + row0;
-  const float* tmp = p.tmp_out + row0 * D;
+  const float* tmp = p.tmp_out + row0 * D + lane * V;
 
   float M = -INFINITY;
-  for (int i = threadIdx.x; i < num_parts; i += kMergeThreads) M = fmaxf(M, ml[i]);
+  for (int i = lane; i < num_parts; i += 32) M = fmaxf(M, ml[i]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if (lane == 0) wmax[warp] = M;
-  __syncthreads();
-  M = wmax[0];
-#pragma unroll
-  for (int w = 1; w < WARPS; ++w) M = fmaxf(M, wmax[w]);
 
   float acc[V];
 #pragma unroll
   for (int j = 0; j < V; ++j) acc[j] = 0.0f;
-  float ws = 0.0f;
+  float wsum = 0.0f;
 #pragma unroll 4
-  for (int i = warp; i < num_parts; i += WARPS) {
+  for (int i = warp; i < num_parts; i += kMergeWarps) {
     const float w = es[i] * fast_exp2((ml[i] - M) * kLog2e);
-    const Vec x = *reinterpret_cast<const Vec*>(tmp + static_cast<int64_t>(i) * D + lane * V);
-    ws += w;
+    const Vec x = *reinterpret_cast<const Vec*>(tmp + static_cast<int64_t>(i) * D);
+    wsum += w;
 #pragma unroll
     for (int j = 0; j < V; ++j) acc[j] = fmaf(w, x.v[j], acc[j]);
   }
 #pragma unroll
   for (int j = 0; j < V; ++j) red[warp][lane * V + j] = acc[j];
-  if (lane == 0) wsum[warp] = ws;
+  if (lane == 0) wsums[warp] = wsum;
   __syncthreads();
   float total = 0.0f;
 #pragma unroll
-  for (int w = 0; w < WARPS; ++w) total += wsum[w];
+  for (int w = 0; w < kMergeWarps; ++w) total += wsums[w];
   const float inv = 1.0f / total;
   for (int d = threadIdx.x; d < D; d += kMergeThreads) {
     float o = 0.0f;
 #pragma unroll
-    for (int w = 0; w < WARPS; ++w) o += red[w][d];
+    for (int w = 0; w < kMergeWarps; ++w) o += red[w][d];
     out[d] = Conv<T>::from_f32(o * inv);
   }
 }

@@ -30,19 +30,15 @@ namespace {
 constexpr int kVersion = 100;  // 0.1.0
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
-// [kMinPartition, kMaxPartition] tokens (overridable for tuning sweeps).
+// at least kMinPartition tokens (overridable for tuning sweeps).
 #ifndef DK_PLAN_CTAS_PER_SM
 #define DK_PLAN_CTAS_PER_SM 2
 #endif
 #ifndef DK_PLAN_MIN_PARTITION
 #define DK_PLAN_MIN_PARTITION 128
 #endif
-#ifndef DK_PLAN_MAX_PARTITION
-#define DK_PLAN_MAX_PARTITION 4096
-#endif
 constexpr int kPlanCtasPerSm = DK_PLAN_CTAS_PER_SM;
 constexpr int kMinPartition = DK_PLAN_MIN_PARTITION;
-constexpr int kMaxPartition = DK_PLAN_MAX_PARTITION;
 
 thread_local char g_last_error[512] = {0};
 
@@ -195,24 +191,31 @@ int validate(const DkPagedAttnArgs* a) {
 // * one sequence (lengths cannot vary): spread its work over ~one wave of
 //   kPlanCtasPerSm CTAs per SM;
 // * several sequences with fewer (sequence, kv_head) pairs than ~4 waves of
-//   CTAs: lengths may vary, so keep partitions <= kVariedPartition tokens
-//   for balance;
-// * many pairs: partitions up to kMaxPartition (plenty of CTAs already).
-// Always a multiple of 64 tokens within [kMinPartition, kMaxPartition].
-#ifndef DK_PLAN_VARIED_PARTITION
-#define DK_PLAN_VARIED_PARTITION 1024
+//   CTAs: lengths may vary, so cap a partition at kVariedBytes of K+V (1024
+//   tokens at head_dim 128, 512 at 256) for balance;
+// * many pairs: partitions up to kMaxBytes of K+V (4096 tokens at 128).
+// Caps are in bytes because a CTA streams a roughly fixed number of bytes
+// per second whatever the head size.  Always a multiple of 64 tokens, at
+// least kMinPartition.
+#ifndef DK_PLAN_VARIED_BYTES
+#define DK_PLAN_VARIED_BYTES (512 * 1024)
 #endif
-constexpr int kVariedPartition = DK_PLAN_VARIED_PARTITION;
+#ifndef DK_PLAN_MAX_BYTES
+#define DK_PLAN_MAX_BYTES (2 * 1024 * 1024)
+#endif
+constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
+constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
 
 int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms) {
-  (void)head_dim;
   const long long pairs = std::max<long long>(1, static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1));
   const long long slots = static_cast<long long>(kPlanCtasPerSm) * sms;
   const long long work = pairs * std::max(max_seq_len, 1);
+  const long long token_bytes = 4LL * head_dim;  // K + V, 16-bit elements
   int ps = round_up((work + slots - 1) / slots, DK_TILE_TOKENS);
-  int cap = kMaxPartition;
-  if (num_seqs > 1 && pairs < 4 * slots) cap = std::min(cap, kVariedPartition);
-  return std::min(std::max(ps, kMinPartition), cap);
+  long long cap = kMaxBytes / token_bytes;
+  if (num_seqs > 1 && pairs < 4 * slots) cap = std::min(cap, kVariedBytes / token_bytes);
+  cap = std::max<long long>(DK_TILE_TOKENS, cap / DK_TILE_TOKENS * DK_TILE_TOKENS);
+  return static_cast<int>(std::min<long long>(std::max(ps, kMinPartition), cap));
 }
 
 // Path choice: the TMA path needs 16-byte aligned bases and strides (the

@@ -22,11 +22,15 @@ struct RedLayout {
   static constexpr int floats(int warps) { return warps * kMaxGroup * kRow + 2 * warps * kMaxGroup; }
 };
 
+// A sequence whose whole length fits in partition 0 needs no merge: its
+// result also goes straight to `out` (the merge kernel skips it), while the
+// workspace row is still written so the workspace keeps the same contents.
 template <typename T, int D, int WARPS>
 __device__ __forceinline__ void write_partition_result(const DecodeParams& p, const float* red_o, const float* red_m,
-                                                       const float* red_l, int seq, int kv_head, int part, int tid,
-                                                       int nthreads) {
+                                                       const float* red_l, int seq, int kv_head, int part, int seq_len,
+                                                       int tid, int nthreads) {
   const int group = p.group;
+  const bool to_out = !p.split || (part == 0 && seq_len <= p.partition_size);
   constexpr int R = RedLayout<D>::kRow;
   for (int idx = tid; idx < group * D; idx += nthreads) {
     const int h = idx / D;
@@ -50,9 +54,8 @@ __device__ __forceinline__ void write_partition_result(const DecodeParams& p, co
         p.max_logits[row] = M * kLn2;
         p.exp_sums[row] = den;
       }
-    } else {
-      static_cast<T*>(p.out)[seq * p.out_stride_seq + q_head * p.out_stride_head + d] = Conv<T>::from_f32(o);
     }
+    if (to_out) static_cast<T*>(p.out)[seq * p.out_stride_seq + q_head * p.out_stride_head + d] = Conv<T>::from_f32(o);
   }
 }
 

@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     }
   }
   __syncthreads();
-  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, threadIdx.x, kSimtThreads);
+  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, seq_len, threadIdx.x,
+                                      kSimtThreads);
 }
 
 }  // namespace dkb

@@ -324,7 +324,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
     red_l[warp * kMaxGroup + c0 + 1] = l1;
   }
   named_bar_sync(1, WARPS * 32);
-  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, threadIdx.x, WARPS * 32);
+  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, seq_len, threadIdx.x, WARPS * 32);
 }
 
 }  // namespace dkb
