@@ -1,0 +1,144 @@
+"""Swap this library's paged-attention decode into vLLM.
+
+The same surface as DecodeKernels' ``decode_kernels/vllm_patch.py`` (``apply``,
+``stats``, ``reset_stats``; ``decode_kernels/vllm_patch.py:47-55,200-211``),
+re-targeted at the vLLM installed here (0.22, v1 engine, FlashAttention
+backend):
+
+* ``FlashAttentionImpl.forward`` -- pure-decode batches (one query token per
+  request) run ``paged_attention_decode`` on vLLM's KV cache in place.  vLLM
+  0.22 stores the cache as ``[2, num_blocks, block_size, num_kv_heads,
+  head_size]`` (any stride order) and splits it with ``kv_cache.unbind(0)``;
+  the kernel reads those two strided views directly.  The reference's patch
+  built its views with ``kv_cache.transpose(1, 2).split(head_size, -1)``
+  for an older interleaved layout (``decode_kernels/vllm_patch.py:122``).
+  vLLM writes the new token's K/V before ``forward`` runs, so ``seq_lens``
+  already includes it.
+* Everything else falls back to the original FlashAttention path through a
+  strict eligibility check (``_attention_eligible``): prefill and mixed
+  batches, quantized KV caches, sliding windows, ALiBi, soft-capping, sinks,
+  cascade attention, context parallelism, CUDA-graph capture, head sizes
+  other than 64/128/256 and GQA groups above 8.
+* ``rms_norm`` and ``silu_and_mul`` (the reference's other two patches) are
+  not part of this library; asking for them logs a note and changes nothing.
+"""
+
+from __future__ import annotations
+
+import logging
+
+import torch
+
+from . import ops as dk_ops
+
+logger = logging.getLogger("decodekernels_b200.vllm")
+
+_STATS = {"attention_kernel_calls": 0, "attention_fallback_calls": 0}
+_APPLIED: set[str] = set()
+_HALF_TYPES = (torch.float16, torch.bfloat16)
+_NOT_PROVIDED = ("rms_norm", "silu_and_mul")
+
+
+def stats() -> dict[str, int]:
+    """How often the patched attention used this library vs fell back."""
+    return dict(_STATS)
+
+
+def reset_stats() -> None:
+    for k in _STATS:
+        _STATS[k] = 0
+
+
+def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_scale, output_block_scale) -> bool:
+    """True when this decode batch can run on decodekernels_b200 unchanged."""
+    if attn_metadata is None or output_scale is not None or output_block_scale is not None:
+        return False
+    if query.is_cuda and torch.cuda.is_current_stream_capturing():
+        # The split-K grid is planned from the host-side max_seq_len; leave
+        # captured graphs to FlashAttention, as the reference does.
+        return False
+    try:
+        from vllm.v1.attention.backend import AttentionType
+
+        decoder = AttentionType.DECODER
+    except ImportError:  # pragma: no cover - depends on the vLLM build
+        decoder = "decoder"
+    if getattr(impl, "attn_type", decoder) != decoder or getattr(attn_metadata, "max_query_len", None) != 1:
+        return False
+    if getattr(attn_metadata, "use_cascade", False):
+        return False
+    if getattr(impl, "dcp_world_size", 1) > 1:
+        return False
+    if str(getattr(impl, "kv_cache_dtype", "auto")) not in ("auto", "float16", "bfloat16"):
+        return False
+    if query.dtype not in _HALF_TYPES or kv_cache.dtype != query.dtype:
+        return False
+    if kv_cache.dim() != 5 or kv_cache.shape[0] != 2:
+        return False
+    if getattr(impl, "alibi_slopes", None) is not None or getattr(impl, "logits_soft_cap", None):
+        return False
+    if getattr(impl, "sliding_window", None) not in (None, (-1, -1)):
+        return False
+    if getattr(impl, "sinks", None) is not None:
+        return False
+    if impl.head_size not in dk_ops.SUPPORTED_HEAD_DIMS:
+        return False
+    if impl.num_heads % impl.num_kv_heads or impl.num_heads // impl.num_kv_heads > dk_ops.MAX_GQA_GROUP:
+        return False
+    if getattr(attn_metadata, "causal", True) is not True:
+        return False
+    n = attn_metadata.num_actual_tokens
+    if attn_metadata.seq_lens.shape[0] < n or attn_metadata.block_table.shape[0] < n:
+        return False
+    if not output.is_contiguous():
+        return False
+    return True
+
+
+def _decode(impl, query, kv_cache, attn_metadata, output) -> torch.Tensor:
+    n = attn_metadata.num_actual_tokens
+    key_cache, value_cache = kv_cache.unbind(0)  # two [blocks, bs, heads, D] views, read in place
+    q = query[:n].reshape(n, impl.num_heads, impl.head_size)
+    out = output[:n].view(n, impl.num_heads, impl.head_size)
+    dk_ops.paged_attention_decode(q, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
+                                  scale=impl.scale, max_seq_len=attn_metadata.max_seq_len, out=out)
+    return output
+
+
+def _patch_attention() -> None:
+    from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+
+    original = FlashAttentionImpl.forward
+
+    def forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale=None,
+                output_block_scale=None):
+        if _attention_eligible(self, query, kv_cache, attn_metadata, output, output_scale, output_block_scale):
+            _STATS["attention_kernel_calls"] += 1
+            return _decode(self, query, kv_cache, attn_metadata, output)
+        _STATS["attention_fallback_calls"] += 1
+        return original(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale,
+                        output_block_scale)
+
+    forward.__wrapped__ = original  # type: ignore[attr-defined]
+    FlashAttentionImpl.forward = forward
+
+
+_PATCHERS = {"attention": _patch_attention}
+
+
+def apply(ops: list[str] | None = None) -> None:
+    """Install the patches (idempotent)."""
+    if not dk_ops.is_available():
+        logger.warning("decodekernels_b200: native library or GPU unavailable; vLLM left unpatched")
+        return
+    for name in ops or list(_PATCHERS):
+        if name in _NOT_PROVIDED:
+            logger.info("decodekernels_b200 provides no %s kernel; vLLM keeps its own", name)
+            continue
+        if name not in _PATCHERS:
+            raise ValueError(f"unknown op {name!r}; choose from {sorted(_PATCHERS)}")
+        if name in _APPLIED:
+            continue
+        _PATCHERS[name]()
+        _APPLIED.add(name)
+    logger.info("decodekernels_b200: patched vLLM ops %s", sorted(_APPLIED))

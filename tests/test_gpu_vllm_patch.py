@@ -1,0 +1,62 @@
+"""GPU: the patched vLLM FlashAttentionImpl.forward runs this library's
+kernels on a vLLM 0.22 KV cache ([2, num_blocks, block_size, num_kv_heads,
+head_size], both stride orders vLLM uses) and matches the oracle."""
+
+from types import SimpleNamespace
+
+import pytest
+import torch
+
+import decodekernels_b200 as dk
+from decodekernels_b200.testing import PagedKV
+from gpu_helpers import assert_attention_close, oracle_dense
+
+vllm = pytest.importorskip("vllm")
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not dk.is_available(), reason="needs a CUDA GPU and the built native library"),
+]
+
+
+@pytest.mark.parametrize("stride_order", ["nhd", "hnd"])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_patched_forward_decodes_on_vllm_cache(stride_order, dtype):
+    from vllm.v1.attention.backend import AttentionType
+    from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+
+    from decodekernels_b200 import vllm_patch
+
+    vllm_patch.apply(["attention"])
+    vllm_patch.reset_stats()
+
+    n, hq, hkv, d, bs = 5, 32, 8, 128, 16
+    lens = [1, 700, 2049, 64, 3000]
+    nb = sum(-(-L // bs) for L in lens) + 4
+    g = torch.Generator(device="cuda").manual_seed(7)
+    if stride_order == "nhd":
+        kv_cache = torch.randn(2, nb, bs, hkv, d, generator=g, device="cuda", dtype=dtype)
+    else:  # physical [2, blocks, heads, bs, D] viewed as vLLM's logical shape
+        kv_cache = torch.randn(2, nb, hkv, bs, d, generator=g, device="cuda", dtype=dtype).transpose(2, 3)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(8)).to(torch.int32)
+    width = max(-(-L // bs) for L in lens)
+    table = torch.zeros(n, width, dtype=torch.int32)
+    off = 0
+    for i, L in enumerate(lens):
+        k = -(-L // bs)
+        table[i, :k] = perm[off:off + k]
+        off += k
+    impl = SimpleNamespace(attn_type=AttentionType.DECODER, dcp_world_size=1, kv_cache_dtype="auto",
+                           alibi_slopes=None, logits_soft_cap=None, sliding_window=None, sinks=None, head_size=d,
+                           num_heads=hq, num_kv_heads=hkv, scale=d**-0.5)
+    meta = SimpleNamespace(max_query_len=1, use_cascade=False, causal=True, num_actual_tokens=n,
+                           seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"), block_table=table.cuda(),
+                           max_seq_len=max(lens))
+    query = torch.randn(n, hq, d, generator=g, device="cuda", dtype=dtype)
+    output = torch.full((n, hq * d), float("nan"), device="cuda", dtype=dtype)
+    ret = FlashAttentionImpl.forward(impl, None, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    assert ret is output
+    assert vllm_patch.stats()["attention_kernel_calls"] == 1
+    k_cache, v_cache = kv_cache.unbind(0)
+    ref = oracle_dense(query, PagedKV(k_cache, v_cache, meta.block_table, meta.seq_lens, bs))
+    assert_attention_close(output.view(n, hq, d), ref, dtype, f"vllm {stride_order}")
