@@ -8,7 +8,7 @@ namespace dkb {
 constexpr int kTileTokens = 64;      // partition-size granularity; every pipeline tile divides it
 constexpr int kSubTokens = 16;       // tokens per consumer warp per tile (mma M)
 constexpr int kSimtThreads = 128;
-constexpr int kMergeThreads = 128;
+constexpr int kMergeThreads = 256;
 constexpr int kMaxGroup = 8;         // query heads per KV head (mma N)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;

@@ -5,13 +5,13 @@
 // zeros when L <= 0.  Sequences with a single live partition were already
 // written to `out` by the partition kernel and are skipped here.
 //
-// One CTA of 4 warps per (query head, sequence).  Every warp finds the max
-// over all live partitions by itself (lane-strided loads + shuffles), then
-// folds the partitions w, w+4, ... with each lane holding head_dim / 32
-// consecutive floats of a partial output (one 8/16/32-byte load per
-// partition, unrolled so several are in flight); one barrier joins the four
-// partial sums.  Launched with programmatic dependent launch: the CTAs start
-// while the partition kernel drains and wait for its results in
+// One CTA of 8 warps per (query head, sequence).  Warp w folds partitions
+// w, w+8, ... in one pass with a running max (rescaling its partial sum when
+// the max grows), each lane holding head_dim / 32 consecutive floats of a
+// partial output (one 8/16/32-byte load per partition, unrolled so several
+// are in flight); the eight (max, sum, output) states are then combined
+// through shared memory.  Launched with programmatic dependent launch: the
+// CTAs start while the partition kernel drains and wait for its results in
 // griddepcontrol.wait.
 #pragma once
 
@@ -32,7 +32,8 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
   constexpr int V = D / 32;
   using Vec = F32Vec<V>;
   __shared__ float red[kMergeWarps][D];
-  __shared__ float wsums[kMergeWarps];
+  __shared__ float wmax[kMergeWarps];
+  __shared__ float wsum[kMergeWarps];
   const int q_head = blockIdx.x;
   const int seq = blockIdx.y;
   const int warp = threadIdx.x >> 5;
@@ -53,35 +54,46 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
   const float* es = p.exp_sums + row0;
   const float* tmp = p.tmp_out + row0 * D + lane * V;
 
-  float M = -INFINITY;
-  for (int i = lane; i < num_parts; i += 32) M = fmaxf(M, ml[i]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-
+  // running state in log2 units: acc = sum_i s_i 2^(m_i - m) o_i, sum = sum_i s_i 2^(m_i - m)
+  float m = -INFINITY, sum = 0.0f;
   float acc[V];
 #pragma unroll
   for (int j = 0; j < V; ++j) acc[j] = 0.0f;
-  float wsum = 0.0f;
 #pragma unroll 4
   for (int i = warp; i < num_parts; i += kMergeWarps) {
-    const float w = es[i] * fast_exp2((ml[i] - M) * kLog2e);
+    const float mi = ml[i] * kLog2e;
+    const float si = es[i];
     const Vec x = *reinterpret_cast<const Vec*>(tmp + static_cast<int64_t>(i) * D);
-    wsum += w;
+    const float mn = fmaxf(m, mi);
+    const float keep = fast_exp2(m - mn);  // 0 on the first partition
+    const float w = si * fast_exp2(mi - mn);
+    m = mn;
+    sum = fmaf(sum, keep, w);
 #pragma unroll
-    for (int j = 0; j < V; ++j) acc[j] = fmaf(w, x.v[j], acc[j]);
+    for (int j = 0; j < V; ++j) acc[j] = fmaf(acc[j], keep, w * x.v[j]);
   }
 #pragma unroll
   for (int j = 0; j < V; ++j) red[warp][lane * V + j] = acc[j];
-  if (lane == 0) wsums[warp] = wsum;
+  if (lane == 0) {
+    wmax[warp] = m;
+    wsum[warp] = sum;
+  }
   __syncthreads();
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, wmax[w]);
+  float f[kMergeWarps];
   float total = 0.0f;
 #pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) total += wsums[w];
+  for (int w = 0; w < kMergeWarps; ++w) {
+    f[w] = fast_exp2(wmax[w] - M);  // 0 for warps without partitions
+    total = fmaf(f[w], wsum[w], total);
+  }
   const float inv = 1.0f / total;
   for (int d = threadIdx.x; d < D; d += kMergeThreads) {
     float o = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kMergeWarps; ++w) o += red[w][d];
+    for (int w = 0; w < kMergeWarps; ++w) o = fmaf(f[w], red[w][d], o);
     out[d] = Conv<T>::from_f32(o * inv);
   }
 }

@@ -119,10 +119,11 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
   }
   pdl_launch_dependents();
 
-  constexpr int R = RedLayout<D>::kRow;
-  float* red_o = simt_smem;
-  float* red_m = red_o + WARPS * kMaxGroup * R;
-  float* red_l = red_m + WARPS * kMaxGroup;
+  using Red = RedLayout<D>;
+  constexpr int R = Red::kRow;
+  float* red_o = Red::o(simt_smem);
+  float* red_m = Red::m(simt_smem, WARPS);
+  float* red_l = Red::l(simt_smem, WARPS);
 #pragma unroll
   for (int h = 0; h < kMaxGroup; ++h) {
     if (h < group) {
@@ -135,8 +136,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     }
   }
   __syncthreads();
-  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, seq_len, threadIdx.x,
-                                      kSimtThreads);
+  write_partition_result<T, D, WARPS>(p, simt_smem, seq, kv_head, part, seq_len, threadIdx.x, kSimtThreads,
+                                      [] { __syncthreads(); });
 }
 
 }  // namespace dkb

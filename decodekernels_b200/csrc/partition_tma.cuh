@@ -159,6 +159,12 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
       __syncwarp();
     }
     pdl_launch_dependents();
+    // The producer then helps with the merge (it holds no partial state).
+    named_bar_sync(1, Cfg::kThreads);
+    named_bar_sync(1, Cfg::kThreads);
+    float* red = reinterpret_cast<float*>(smem);
+    write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
+                                        [] { named_bar_sync(1, Cfg::kThreads); });
     return;
   }
 
@@ -301,12 +307,14 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   }
 
   // Every tile's TMA writes have landed (warp 0 waits on every tile), so the
-  // ring can be reused for the cross-warp merge once all consumers are here.
-  named_bar_sync(1, WARPS * 32);
-  constexpr int R = RedLayout<D>::kRow;
-  float* red_o = reinterpret_cast<float*>(smem);
-  float* red_m = red_o + WARPS * kMaxGroup * R;
-  float* red_l = red_m + WARPS * kMaxGroup;
+  // ring can be reused for the cross-warp merge once all warps are here.
+  named_bar_sync(1, Cfg::kThreads);
+  using Red = RedLayout<D>;
+  constexpr int R = Red::kRow;
+  float* red = reinterpret_cast<float*>(smem);
+  float* red_o = Red::o(red);
+  float* red_m = Red::m(red, WARPS);
+  float* red_l = Red::l(red, WARPS);
   const int c0 = 2 * (lane & 3);
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
@@ -323,8 +331,9 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
     red_l[warp * kMaxGroup + c0] = l0;
     red_l[warp * kMaxGroup + c0 + 1] = l1;
   }
-  named_bar_sync(1, WARPS * 32);
-  write_partition_result<T, D, WARPS>(p, red_o, red_m, red_l, seq, kv_head, part, seq_len, threadIdx.x, WARPS * 32);
+  named_bar_sync(1, Cfg::kThreads);
+  write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
+                                      [] { named_bar_sync(1, Cfg::kThreads); });
 }
 
 }  // namespace dkb
