@@ -33,6 +33,7 @@ struct DecodeParams {
   int64_t bt_stride;
   int num_q_heads;
   int group;           // num_q_heads / num_kv_heads
+  int max_seq_len;     // host-side bound on seq_lens; longer lengths count as this
   int block_size;
   int num_blocks;      // cache blocks; ids outside [0, num_blocks) read as zeros
   int bs_log2;         // log2(block_size) (TMA path: power-of-two block sizes)

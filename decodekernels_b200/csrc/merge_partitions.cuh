@@ -27,28 +27,17 @@ struct alignas(4 * N) F32Vec {
 
 constexpr int kMergeWarps = kMergeThreads / 32;
 
+// Fold workspace rows [0, num_rows) of (seq, q_head) into `out` (all threads
+// of the CTA take part).
 template <typename T, int D>
-__global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const DecodeParams p) {
+__device__ __forceinline__ void merge_rows(const DecodeParams& p, int seq, int q_head, int num_rows, T* out) {
   constexpr int V = D / 32;
   using Vec = F32Vec<V>;
   __shared__ float red[kMergeWarps][D];
   __shared__ float wmax[kMergeWarps];
   __shared__ float wsum[kMergeWarps];
-  const int q_head = blockIdx.x;
-  const int seq = blockIdx.y;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  pdl_wait_primary();
-  T* out = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head;
-  const int seq_len = p.seq_lens[seq];
-  if (seq_len <= 0) {
-    for (int d = threadIdx.x; d < D; d += kMergeThreads) out[d] = Conv<T>::from_f32(0.0f);
-    return;
-  }
-  const int num_parts = min((seq_len + p.partition_size - 1) / p.partition_size, p.num_partitions);
-  if (num_parts <= 1) return;  // written by the partition kernel
-
   const int64_t row0 = (static_cast<int64_t>(seq) * p.num_q_heads + q_head) * p.ws_partitions;
   const float* ml = p.max_logits + row0;
   const float* es = p.exp_sums + row0;
@@ -60,12 +49,12 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
 #pragma unroll
   for (int j = 0; j < V; ++j) acc[j] = 0.0f;
 #pragma unroll 4
-  for (int i = warp; i < num_parts; i += kMergeWarps) {
+  for (int i = warp; i < num_rows; i += kMergeWarps) {
     const float mi = ml[i] * kLog2e;
     const float si = es[i];
     const Vec x = *reinterpret_cast<const Vec*>(tmp + static_cast<int64_t>(i) * D);
     const float mn = fmaxf(m, mi);
-    const float keep = fast_exp2(m - mn);  // 0 on the first partition
+    const float keep = fast_exp2(m - mn);  // 0 on the first row
     const float w = si * fast_exp2(mi - mn);
     m = mn;
     sum = fmaf(sum, keep, w);
@@ -86,7 +75,7 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
   float total = 0.0f;
 #pragma unroll
   for (int w = 0; w < kMergeWarps; ++w) {
-    f[w] = fast_exp2(wmax[w] - M);  // 0 for warps without partitions
+    f[w] = fast_exp2(wmax[w] - M);  // 0 for warps without rows
     total = fmaf(f[w], wsum[w], total);
   }
   const float inv = 1.0f / total;
@@ -96,6 +85,22 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
     for (int w = 0; w < kMergeWarps; ++w) o = fmaf(f[w], red[w][d], o);
     out[d] = Conv<T>::from_f32(o * inv);
   }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const DecodeParams p) {
+  const int q_head = blockIdx.x;
+  const int seq = blockIdx.y;
+  pdl_wait_primary();
+  T* out = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head;
+  const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
+  if (seq_len <= 0) {
+    for (int d = threadIdx.x; d < D; d += kMergeThreads) out[d] = Conv<T>::from_f32(0.0f);
+    return;
+  }
+  const int num_parts = min((seq_len + p.partition_size - 1) / p.partition_size, p.num_partitions);
+  if (num_parts <= 1) return;  // written by the partition kernel
+  merge_rows<T, D>(p, seq, q_head, num_parts, out);
 }
 
 }  // namespace dkb

@@ -405,6 +405,22 @@ cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, int smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// K and V tensor maps (one map for both when K|V rows are interleaved).
+template <int D>
+int build_maps(const DkPagedAttnArgs& a, DecodeParams& p, int dev, CUtensorMap* kmap, CUtensorMap* vmap) {
+  const int rows = 1 << p.rows_log2;
+  p.kv_fused = kv_fused(a) ? 1 : 0;
+  if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
+                        a.num_kv_heads, (p.kv_fused ? 2 : 1) * (D / 64), rows, dev, kmap))
+    return r;
+  if (p.kv_fused) {
+    *vmap = *kmap;  // unused
+    return 0;
+  }
+  return build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks, a.block_size,
+                   a.num_kv_heads, D / 64, rows, dev, vmap);
+}
+
 template <typename T, int D>
 int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(pl.num_partitions), static_cast<unsigned>(a.num_kv_heads),
@@ -418,17 +434,7 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
     e = ensure_smem_attr(kernel, smem, dev, attr_done);
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(partition kernel)");
     CUtensorMap kmap, vmap;
-    const int rows = 1 << p.rows_log2;
-    p.kv_fused = kv_fused(a) ? 1 : 0;
-    if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
-                          a.num_kv_heads, (p.kv_fused ? 2 : 1) * (D / 64), rows, dev, &kmap))
-      return r;
-    if (p.kv_fused) {
-      vmap = kmap;  // unused
-    } else if (int r = build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks,
-                                 a.block_size, a.num_kv_heads, D / 64, rows, dev, &vmap)) {
-      return r;
-    }
+    if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
     e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
     if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch");
   } else {
@@ -469,6 +475,7 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.bt_stride = a.bt_stride;
   p.num_q_heads = a.num_q_heads;
   p.group = a.num_q_heads / a.num_kv_heads;
+  p.max_seq_len = a.max_seq_len;
   p.block_size = a.block_size;
   p.num_blocks = a.num_blocks;
   p.bs_log2 = ilog2(a.block_size);
@@ -596,8 +603,8 @@ int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_d
     cudaGetLastError();
     dev = -1;
   }
-  const int ps = dkb::desired_partition_size(num_seqs, num_kv_heads <= 0 ? 1 : num_kv_heads, head_dim, max_seq_len,
-                                             dkb::num_sms(dev));
+  const int hkv = num_kv_heads <= 0 ? 1 : num_kv_heads;
+  const int ps = dkb::desired_partition_size(num_seqs, hkv, head_dim, max_seq_len, dkb::num_sms(dev));
   return dkb::ceil_div(max_seq_len, ps);
 }
 

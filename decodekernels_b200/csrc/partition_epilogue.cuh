@@ -29,17 +29,15 @@ struct RedLayout {
   static __device__ __forceinline__ float* head(float* red, int warps) { return fac(red, warps) + warps * kMaxGroup; }
 };
 
-// Merge the WARPS per-warp states already in `red` and write the partition
-// result.  The per-head factors are computed once (by `group` threads), then
-// every thread produces 4 consecutive outputs.  `sync` is the barrier of the
-// `nthreads` participating threads.
-//
-// A sequence whose whole length fits in partition 0 needs no merge: its
-// result also goes straight to `out` (the merge kernel skips it), while the
-// workspace row is still written so the workspace keeps the same contents.
+// Merge the WARPS per-warp states already in `red` and write the result of
+// this (sequence, kv_head) partition: to workspace row
+// (seq * Hq + q_head) * ws_partitions + row when `to_ws`, and to `out` when
+// `to_out`.  The per-head factors are computed once (by `group` threads),
+// then every thread produces 4 consecutive outputs.  `sync` is the barrier of
+// the `nthreads` participating threads.
 template <typename T, int D, int WARPS, typename Sync>
-__device__ __forceinline__ void write_partition_result(const DecodeParams& p, float* red, int seq, int kv_head,
-                                                       int part, int seq_len, int tid, int nthreads, Sync sync) {
+__device__ __forceinline__ void write_merged_result(const DecodeParams& p, float* red, int seq, int kv_head, int row,
+                                                    bool to_ws, bool to_out, int tid, int nthreads, Sync sync) {
   using L = RedLayout<D>;
   constexpr int R = L::kRow;
   const int group = p.group;
@@ -66,7 +64,6 @@ __device__ __forceinline__ void write_partition_result(const DecodeParams& p, fl
     head[kMaxGroup + tid] = den;
   }
   sync();
-  const bool to_out = !p.split || (part == 0 && seq_len <= p.partition_size);
   constexpr int Q = D / 4;
   for (int idx = tid; idx < group * Q; idx += nthreads) {
     const int h = idx / Q;
@@ -82,12 +79,12 @@ __device__ __forceinline__ void write_partition_result(const DecodeParams& p, fl
       o.w = fmaf(f, x.w, o.w);
     }
     const int q_head = kv_head * group + h;
-    if (p.split) {
-      const int64_t row = (static_cast<int64_t>(seq) * p.num_q_heads + q_head) * p.ws_partitions + part;
-      *reinterpret_cast<float4*>(p.tmp_out + row * D + d) = o;
+    if (to_ws) {
+      const int64_t wrow = (static_cast<int64_t>(seq) * p.num_q_heads + q_head) * p.ws_partitions + row;
+      *reinterpret_cast<float4*>(p.tmp_out + wrow * D + d) = o;
       if (d == 0) {
-        p.max_logits[row] = head[h] * kLn2;
-        p.exp_sums[row] = head[kMaxGroup + h];
+        p.max_logits[wrow] = head[h] * kLn2;
+        p.exp_sums[wrow] = head[kMaxGroup + h];
       }
     }
     if (to_out) {
@@ -98,6 +95,17 @@ __device__ __forceinline__ void write_partition_result(const DecodeParams& p, fl
       dst[3] = Conv<T>::from_f32(o.w);
     }
   }
+}
+
+// Result of partition `part` of the partition kernels.  A
+// sequence whose whole length fits in partition 0 needs no merge: its result
+// also goes straight to `out` (the merge kernel skips it), while the
+// workspace row is still written so the workspace keeps the same contents.
+template <typename T, int D, int WARPS, typename Sync>
+__device__ __forceinline__ void write_partition_result(const DecodeParams& p, float* red, int seq, int kv_head,
+                                                       int part, int seq_len, int tid, int nthreads, Sync sync) {
+  const bool to_out = !p.split || (part == 0 && seq_len <= p.partition_size);
+  write_merged_result<T, D, WARPS>(p, red, seq, kv_head, part, p.split != 0, to_out, tid, nthreads, sync);
 }
 
 // Zeros for the group's query heads of an empty sequence (single-pass path),

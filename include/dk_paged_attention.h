@@ -98,7 +98,7 @@ typedef struct DkPagedAttnArgs {
   int64_t bt_stride;
   int32_t num_seqs, num_q_heads, num_kv_heads, head_dim, block_size;
   int32_t num_blocks;     /* size of the caches' first dim; ids outside [0, num_blocks) read zeros on the TMA path */
-  int32_t max_seq_len;    /* host-side upper bound on seq_lens; shapes the grid */
+  int32_t max_seq_len;    /* host-side upper bound on seq_lens; shapes the grid (longer lengths count as this) */
   int32_t max_partitions; /* workspace capacity (tmp_out.size(2)); 0 = no workspace */
   int32_t partition_size; /* 0 = planner's choice; else a multiple of 64 tokens */
   int32_t dtype;          /* DK_DTYPE_* */

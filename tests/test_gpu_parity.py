@@ -184,9 +184,10 @@ def test_block_sizes_tma_path(block_size, dtype):
     seq_lens = [1, 63, 64, 65, 700, 1500]
     kv = make_paged_kv(seq_lens, 2, 128, block_size, dtype, "cuda", seed=block_size)
     q = _q(len(seq_lens), 8, 128, dtype, seed=block_size)
-    out, _, plan = run_capi(q, kv)
-    assert plan["path"] == capi.DK_PATH_TMA_MMA
-    assert_attention_close(out, oracle_dense(q, kv), dtype, f"bs={block_size}")
+    for ps in (0, 64, 512):
+        out, _, plan = run_capi(q, kv, partition_size=ps)
+        assert plan["path"] == capi.DK_PATH_TMA_MMA
+        assert_attention_close(out, oracle_dense(q, kv), dtype, f"bs={block_size} ps={ps}")
 
 
 @pytest.mark.parametrize("block_size", [1, 3, 12, 48])
@@ -258,16 +259,79 @@ def test_partition_sizes_agree(head_dim):
 
 
 def test_max_seq_len_below_actual_clamps_like_reference():
-    """A too-small max_seq_len never reads out of bounds: single pass attends
-    to the first max_seq_len tokens rounded up to the tile (the reference
-    clamps at its 512-token partition)."""
+    """A too-small max_seq_len never reads out of bounds: lengths above it
+    count as max_seq_len on every path, so no block-table entry at or past
+    ceil(max_seq_len / block_size) is read.  (The reference's partition
+    kernel takes its 512-token partition up to seq_len there, reading past
+    a block table sized for max_seq_len.)"""
     kv = make_paged_kv([300], 1, 64, 16, torch.float16, "cuda")
     q = _q(1, 4, 64, torch.float16)
-    out, _, plan = run_capi(q, kv, max_seq_len=100, workspace=None)
-    kv.seq_lens.fill_(128)
-    assert_attention_close(out, oracle_dense(q, kv), torch.float16, "clamped")
+    for kwargs in ({"workspace": None}, {"partition_size": 64}, {}, {"force_simt": True}):
+        out, _, plan = run_capi(q, kv, max_seq_len=100, **kwargs)
+        kv.seq_lens.fill_(100)
+        assert_attention_close(out, oracle_dense(q, kv), torch.float16, f"clamped {kwargs}")
+        kv.seq_lens.fill_(300)
 
 
 def test_no_wait_timeouts():
     """No bounded device wait gave up during this session."""
     assert capi.wait_timeouts(0) == 0
+
+
+# ---------------------------------------------------------------------------
+# Planner: mixed lengths, workspace capacity, batch sizes
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("head_dim,group,layout", [(128, 8, "vllm"), (128, 4, "hnd"), (64, 1, "nhd"), (256, 8, "nhd")])
+def test_planner_varied_lengths(dtype, head_dim, group, layout):
+    """Mixed lengths with empty sequences and one long one, at the planner's
+    partition size and at the smallest (one tile per partition)."""
+    g = torch.Generator().manual_seed(head_dim + group)
+    lens = torch.randint(1, 3000, (37,), generator=g).tolist()
+    lens[3] = lens[20] = 0
+    lens[7] = 9000
+    kv = make_paged_kv(lens, 2, head_dim, 16, dtype, "cuda", layout=layout, seed=group)
+    q = _q(len(lens), 2 * group, head_dim, dtype, seed=head_dim)
+    for ps in (0, 64):
+        out, _, plan = run_capi(q, kv, partition_size=ps)
+        assert plan["path"] == capi.DK_PATH_TMA_MMA and plan["split"] == 1
+        out_np = out.float().cpu()
+        assert torch.count_nonzero(out_np[3]) == 0 and torch.count_nonzero(out_np[20]) == 0
+        assert_attention_close(out, oracle_dense(q, kv), dtype, f"varied ps={ps}")
+
+
+@pytest.mark.parametrize("rows", [2, 3, 5])
+def test_planner_small_workspace_grows_partitions(rows):
+    """A workspace with fewer rows than the planner wants: partitions grow
+    so ceil(max_seq_len / partition_size) fits."""
+    lens = [20000, 5, 3000, 64]
+    kv = make_paged_kv(lens, 2, 128, 16, torch.bfloat16, "cuda", seed=rows)
+    q = _q(len(lens), 16, 128, torch.bfloat16)
+    ws = alloc_ws(len(lens), 16, 128, rows, q.device)
+    out, _, plan = run_capi(q, kv, workspace=ws)
+    assert plan["path"] == capi.DK_PATH_TMA_MMA and plan["num_partitions"] <= rows
+    assert plan["num_partitions"] * plan["partition_size"] >= 20000
+    assert_attention_close(out, oracle_dense(q, kv), torch.bfloat16, f"{rows} rows")
+
+
+def test_planner_matches_fixed_partitions():
+    """The planner's split and the reference's 512-token split agree to
+    fp32 rounding (same math, different partition boundaries)."""
+    lens = [1, 63, 64, 65, 511, 512, 513, 4000, 12000, 0, 777]
+    kv = make_paged_kv(lens, 4, 128, 32, torch.float16, "cuda", layout="vllm", seed=5)
+    q = _q(len(lens), 32, 128, torch.float16)
+    a, _, pa = run_capi(q, kv)
+    b, _, pb = run_capi(q, kv, partition_size=512)
+    assert pa["path"] == pb["path"] == capi.DK_PATH_TMA_MMA
+    assert (a.float() - b.float()).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("n", [1024, 4099])
+def test_planner_large_batches(n):
+    g = torch.Generator().manual_seed(n)
+    lens = torch.randint(0, 200, (n,), generator=g).tolist()
+    kv = make_paged_kv(lens, 1, 64, 16, torch.bfloat16, "cuda", seed=n)
+    q = _q(n, 4, 64, torch.bfloat16)
+    out, _, plan = run_capi(q, kv)
+    assert plan["path"] == capi.DK_PATH_TMA_MMA
+    assert_attention_close(out, oracle_dense(q, kv), torch.bfloat16, f"n={n}")
