@@ -265,7 +265,7 @@ def run_gpu_arm(args) -> None:
     max_len = batch.max_seq_len
     out = torch.empty_like(q)
     ws = dk.alloc_workspace(n, hq, d, max_len, dev, num_kv_heads=kv.k_cache.shape[2],
-                            block_size=kv.block_size)
+                            block_size=kv.block_size, merge_counters=True)
     plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, ws)
 
     def step():

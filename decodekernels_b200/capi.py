@@ -22,6 +22,7 @@ DK_DTYPE_FLOAT16 = 0
 DK_DTYPE_BFLOAT16 = 1
 DK_PATH_NONE, DK_PATH_TMA_MMA, DK_PATH_SIMT = 0, 1, 2
 DK_FLAG_FORCE_SIMT = 1
+DK_FLAG_FORCE_FUSED_MERGE = 2
 DK_MAX_GQA_GROUP = 8
 DK_TILE_TOKENS = 64
 DK_REF_PARTITION_SIZE = 512
@@ -43,6 +44,7 @@ class DkPagedAttnArgs(ctypes.Structure):
         ("tmp_out", ctypes.c_void_p),
         ("max_logits", ctypes.c_void_p),
         ("exp_sums", ctypes.c_void_p),
+        ("merge_counters", ctypes.c_void_p),
         ("q_stride_seq", ctypes.c_int64),
         ("q_stride_head", ctypes.c_int64),
         ("out_stride_seq", ctypes.c_int64),
@@ -151,7 +153,7 @@ def _dtype_code(t) -> int:
 
 
 def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-              partition_size: int = 0, force_simt: bool = False) -> DkPagedAttnArgs:
+              partition_size: int = 0, force_simt: bool = False, flags: int = 0) -> DkPagedAttnArgs:
     """Fill the C struct from tensors (pointers + element strides)."""
     a = DkPagedAttnArgs()
     a.out = out.data_ptr()
@@ -161,9 +163,11 @@ def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, o
     a.block_tables = block_tables.data_ptr()
     a.seq_lens = seq_lens.data_ptr()
     if workspace is not None and workspace[0].numel() > 0:
-        tmp_out, max_logits, exp_sums = workspace
+        tmp_out, max_logits, exp_sums = workspace[:3]
         a.tmp_out, a.max_logits, a.exp_sums = tmp_out.data_ptr(), max_logits.data_ptr(), exp_sums.data_ptr()
         a.max_partitions = tmp_out.shape[2]
+        if len(workspace) > 3 and workspace[3] is not None and workspace[3].numel() > 0:
+            a.merge_counters = workspace[3].data_ptr()  # single-launch merge
     a.q_stride_seq, a.q_stride_head = q.stride(0), q.stride(1)
     a.out_stride_seq, a.out_stride_head = out.stride(0), out.stride(1)
     a.k_stride_block, a.k_stride_token, a.k_stride_head = k_cache.stride()[:3]
@@ -176,15 +180,15 @@ def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, o
     a.max_seq_len = int(max_seq_len)
     a.partition_size = int(partition_size)
     a.dtype = _dtype_code(q)
-    a.flags = DK_FLAG_FORCE_SIMT if force_simt else 0
+    a.flags = (DK_FLAG_FORCE_SIMT if force_simt else 0) | flags
     a.scale = float(scale)
     return a
 
 
 def plan(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-         partition_size: int = 0, force_simt: bool = False) -> dict:
+         partition_size: int = 0, force_simt: bool = False, flags: int = 0) -> dict:
     a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
-                  force_simt)
+                  force_simt, flags)
     p = DkPlan()
     rc = load().dk_plan(ctypes.byref(a), ctypes.byref(p))
     if rc != 0:
@@ -193,14 +197,14 @@ def plan(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, w
 
 
 def decode(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-           partition_size: int = 0, force_simt: bool = False, stream=None) -> int:
+           partition_size: int = 0, force_simt: bool = False, stream=None, flags: int = 0) -> int:
     """dk_paged_attention_decode on ``stream`` (default: torch's current stream).
 
     Returns 0; raises RuntimeError with the library's message otherwise."""
     import torch
 
     a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
-                  force_simt)
+                  force_simt, flags)
     if stream is None:
         stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
     rc = load().dk_paged_attention_decode(ctypes.byref(a), ctypes.c_void_p(stream))

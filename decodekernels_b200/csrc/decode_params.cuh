@@ -26,12 +26,14 @@ struct DecodeParams {
   float* tmp_out;
   float* max_logits;
   float* exp_sums;
+  int* merge_counters;  // non-null: the last partition of each (seq, kv_head) merges (no merge kernel)
   int64_t q_stride_seq, q_stride_head;
   int64_t out_stride_seq, out_stride_head;
   int64_t k_stride_block, k_stride_token, k_stride_head;
   int64_t v_stride_block, v_stride_token, v_stride_head;
   int64_t bt_stride;
   int num_q_heads;
+  int num_kv_heads;
   int group;           // num_q_heads / num_kv_heads
   int max_seq_len;     // host-side bound on seq_lens; longer lengths count as this
   int block_size;

@@ -27,7 +27,7 @@
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 100;  // 0.1.0
+constexpr int kVersion = 200;  // 0.2.0: DkPagedAttnArgs.merge_counters
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
 // at least kMinPartition tokens (overridable for tuning sweeps).
@@ -180,6 +180,10 @@ int validate(const DkPagedAttnArgs* a) {
     return fail(1, "KV-cache pointers must be aligned to head_dim / 16 bytes");
   if (a->max_partitions > 0 && (!a->tmp_out || !a->max_logits || !a->exp_sums))
     return fail(1, "split-K workspace pointers are NULL but max_partitions > 0");
+  if (a->max_partitions > 0 && (!aligned(a->tmp_out, 16) || !aligned(a->max_logits, 4) || !aligned(a->exp_sums, 4)))
+    return fail(1, "split-K workspace: tmp_out must be 16-byte aligned, max_logits / exp_sums 4-byte aligned");
+  if (a->merge_counters != nullptr && !aligned(a->merge_counters, 4))
+    return fail(1, "merge_counters must be 4-byte aligned");
   return 0;
 }
 
@@ -203,6 +207,10 @@ int validate(const DkPagedAttnArgs* a) {
 #ifndef DK_PLAN_MAX_BYTES
 #define DK_PLAN_MAX_BYTES (2 * 1024 * 1024)
 #endif
+#ifndef DK_FUSED_MERGE_MAX_BYTES
+#define DK_FUSED_MERGE_MAX_BYTES (64 * 1024)
+#endif
+constexpr long long kFusedMergeMaxBytes = DK_FUSED_MERGE_MAX_BYTES;
 constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
 constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
 
@@ -284,7 +292,17 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
                    ? (a.head_dim == 64 ? tma_stages<64>() : (a.head_dim == 128 ? tma_stages<128>() : tma_stages<256>()))
                    : 0;
   pl->smem_bytes = smem_for(pl->path, a.head_dim);
-  pl->launches = pl->split ? 2 : 1;
+  // Merge counters turn the merge into the last partition's epilogue, which
+  // saves the merge kernel's launch and latency but costs every partition a
+  // release + atomic round trip and leaves each pair's merge to one CTA.
+  // Measured worth it for a grid of about one wave whose pairs have a few KB
+  // of rows (c1: 13.3 -> 12.x us); multi-wave grids (c2) and large merges
+  // (c3, c4) are faster with the separate kernel.
+  const long long merge_bytes = 1LL * parts * (a.num_q_heads / a.num_kv_heads) * (a.head_dim + 2) * 4;
+  const long long one_wave = static_cast<long long>(kPlanCtasPerSm) * num_sms(dev);
+  const bool small = merge_bytes <= kFusedMergeMaxBytes && pl->num_ctas <= one_wave;
+  const bool fused = pl->split && a.merge_counters != nullptr && (small || (a.flags & DK_FLAG_FORCE_FUSED_MERGE));
+  pl->launches = pl->split && !fused ? 2 : 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -442,7 +460,7 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
     e = launch_pdl(kernel, grid, dim3(kSimtThreads), SimtConfig<D>::kSmemBytes, stream, p);
     if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch (CUDA-core path)");
   }
-  if (pl.split) {
+  if (pl.split && p.merge_counters == nullptr) {
     const dim3 mgrid(static_cast<unsigned>(a.num_q_heads), static_cast<unsigned>(a.num_seqs));
     e = launch_pdl(merge_partitions_kernel<T, D>, mgrid, dim3(kMergeThreads), 0, stream, p);
     if (e != cudaSuccess) return fail_cuda(e, "merge kernel launch");
@@ -462,6 +480,7 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.tmp_out = pl.split ? a.tmp_out : nullptr;
   p.max_logits = pl.split ? a.max_logits : nullptr;
   p.exp_sums = pl.split ? a.exp_sums : nullptr;
+  p.merge_counters = pl.split && pl.launches == 1 ? a.merge_counters : nullptr;
   p.q_stride_seq = a.q_stride_seq;
   p.q_stride_head = a.q_stride_head;
   p.out_stride_seq = a.out_stride_seq;
@@ -474,6 +493,7 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.v_stride_head = a.v_stride_head;
   p.bt_stride = a.bt_stride;
   p.num_q_heads = a.num_q_heads;
+  p.num_kv_heads = a.num_kv_heads;
   p.group = a.num_q_heads / a.num_kv_heads;
   p.max_seq_len = a.max_seq_len;
   p.block_size = a.block_size;
@@ -506,22 +526,33 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
 // address comes from cudaGetSymbolAddress, once per device.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) float g_noalloc_scratch[DK_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+// Merge counters of the no-allocation path (zero at load; every completed
+// call leaves them zero).  Calls with more (sequence, KV head) pairs use the
+// separate merge kernel.
+constexpr int kNoallocCounters = 1 << 18;
+static __device__ __align__(256) int g_noalloc_counters[kNoallocCounters];
 
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+int* g_noalloc_ctr[kMaxDevices] = {nullptr};
 
-// Device address of the scratch on `dev` (the current device), looked up on
-// the first call for that device.
-int noalloc_scratch(int dev, float** out) {
+// Device addresses of the scratch and the counters on `dev` (the current
+// device), looked up on the first call for that device.
+int noalloc_scratch(int dev, float** out, int** counters) {
   if (dev < 0 || dev >= kMaxDevices) return fail(1, "device %d out of range for the no-allocation scratch", dev);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) return fail_cuda(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    void* c = nullptr;
+    e = cudaGetSymbolAddress(&c, g_noalloc_counters);
+    if (e != cudaSuccess || c == nullptr) return fail_cuda(e, "cudaGetSymbolAddress(no-allocation counters)");
+    g_noalloc_ctr[dev] = static_cast<int*>(c);
     g_noalloc_ptr[dev] = static_cast<float*>(p);
   }
   *out = g_noalloc_ptr[dev];
+  *counters = g_noalloc_ctr[dev];
   return 0;
 }
 
@@ -559,6 +590,7 @@ int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t s
   // partitioning (and the result) is the same as dk_paged_attention_decode's.
   DkPagedAttnArgs a = *args;
   a.max_partitions = INT_MAX;
+  a.merge_counters = nullptr;
   DkPlan pl;
   dkb::make_plan(a, dev, &pl);
   a.max_partitions = 0;
@@ -572,11 +604,19 @@ int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t s
                        "scratch holds %u bytes; call dk_paged_attention_decode with a caller-allocated workspace",
                        need, a.num_seqs, a.num_q_heads, pl.num_partitions, DK_NOALLOC_SCRATCH_BYTES);
     float* base = nullptr;
-    if (int e = dkb::noalloc_scratch(dev, &base)) return e;
+    int* counters = nullptr;
+    if (int e = dkb::noalloc_scratch(dev, &base, &counters)) return e;
     a.tmp_out = base;
     a.max_logits = base + rows * a.head_dim;
     a.exp_sums = a.max_logits + rows;
     a.max_partitions = pl.num_partitions;
+    if (static_cast<long long>(a.num_seqs) * a.num_kv_heads <= dkb::kNoallocCounters) {
+      a.merge_counters = counters;  // one launch when the merge is small
+      const int fixed = a.partition_size;
+      a.partition_size = pl.partition_size;  // same partitions; only the merge choice is re-planned
+      dkb::make_plan(a, dev, &pl);
+      a.partition_size = fixed;
+    }
   }
   return dkb::launch(a, pl, dev, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -97,6 +97,114 @@ __device__ __forceinline__ void write_merged_result(const DecodeParams& p, float
   }
 }
 
+// Shared state of the single-launch merge, one copy per CTA for every caller
+// (a variable inside a function templated on the barrier type would exist
+// once per instantiation, and the producer and consumer warps pass different
+// lambdas): [0] the "this partition merges" flag, then per head of the group
+// the max logit (log2 units) and 1 / exp-sum.
+__device__ __forceinline__ float* merge_shared() {
+  __shared__ float s_merge[1 + 2 * kMaxGroup];
+  return s_merge;
+}
+
+// Counter increment with release (this CTA's prior global writes, ordered
+// before it by the CTA barrier, are visible first) and acquire (the other
+// partitions' writes are visible after it) semantics at GPU scope.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Single-launch merge (p.merge_counters set): every live partition of
+// (seq, kv_head) publishes its workspace rows with one counter increment
+// (after the CTA barrier, release semantics); the partition that brings the
+// count to the number of live partitions merges the group's rows into `out`
+// and resets the counter to 0 for the next call.  No thread waits on another
+// CTA.  The merge keeps every load independent: per head (one warp, a row
+// per lane) the max logit and exp-sum, then every thread sums w_i * o_i for
+// 4 output columns, 8 rows in flight at a time.  Rows are read through L2
+// (ld.global.cg): other CTAs wrote them.
+template <typename T, int D, typename Sync>
+__device__ __forceinline__ void merge_if_last(const DecodeParams& p, int seq, int kv_head, int live, int tid,
+                                              int nthreads, Sync sync) {
+  float* sh = merge_shared();
+  sync();  // every thread's workspace stores precede the release below
+  if (tid == 0) {
+    int* ctr = p.merge_counters + static_cast<int64_t>(seq) * p.num_kv_heads + kv_head;
+    const int last = atomic_add_acq_rel_gpu(ctr, 1) == live - 1;
+    if (last) *ctr = 0;  // every live partition has counted: nothing else touches it in this call
+    sh[0] = last ? 1.0f : 0.0f;
+  }
+  sync();
+  if (sh[0] == 0.0f) return;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int group = p.group;
+  const int64_t head0 = static_cast<int64_t>(seq) * p.num_q_heads + kv_head * group;  // first q-head of the group
+  for (int h = warp; h < group; h += nthreads >> 5) {
+    const float* ml = p.max_logits + (head0 + h) * p.ws_partitions;
+    const float* es = p.exp_sums + (head0 + h) * p.ws_partitions;
+    float m = -INFINITY, w = 0.0f;  // lane-local running (max, sum) over rows lane, lane + 32, ...
+    for (int i = lane; i < live; i += 32) {
+      const float mi = __ldcg(ml + i) * kLog2e;
+      const float si = __ldcg(es + i);
+      const float mn = fmaxf(m, mi);
+      w = fmaf(w, fast_exp2(m - mn), si * fast_exp2(mi - mn));
+      m = mn;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+      const float wo = __shfl_xor_sync(0xffffffffu, w, o);
+      const float mn = fmaxf(m, mo);
+      w = (mn == -INFINITY) ? 0.0f : w * fast_exp2(m - mn) + wo * fast_exp2(mo - mn);
+      m = mn;
+    }
+    if (lane == 0) {
+      sh[1 + h] = m;
+      sh[1 + kMaxGroup + h] = 1.0f / w;
+    }
+  }
+  sync();
+  constexpr int Q = D / 4;
+  constexpr int kBatch = 8;
+  for (int idx = tid; idx < group * Q; idx += nthreads) {
+    const int h = idx / Q;
+    const int d = (idx - h * Q) * 4;
+    const int64_t row0 = (head0 + h) * p.ws_partitions;
+    const float m2 = sh[1 + h];
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int i0 = 0; i0 < live; i0 += kBatch) {
+      float wi[kBatch];
+      float4 x[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        wi[k] = 0.0f;
+        x[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i0 + k < live) {
+          const int64_t r = row0 + i0 + k;
+          wi[k] = __ldcg(p.exp_sums + r) * fast_exp2(fmaf(__ldcg(p.max_logits + r), kLog2e, -m2));
+          x[k] = __ldcg(reinterpret_cast<const float4*>(p.tmp_out + r * D + d));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        acc.x = fmaf(wi[k], x[k].x, acc.x);
+        acc.y = fmaf(wi[k], x[k].y, acc.y);
+        acc.z = fmaf(wi[k], x[k].z, acc.z);
+        acc.w = fmaf(wi[k], x[k].w, acc.w);
+      }
+    }
+    const float inv = sh[1 + kMaxGroup + h];
+    T* dst = static_cast<T*>(p.out) + seq * p.out_stride_seq + (kv_head * group + h) * p.out_stride_head + d;
+    dst[0] = Conv<T>::from_f32(acc.x * inv);
+    dst[1] = Conv<T>::from_f32(acc.y * inv);
+    dst[2] = Conv<T>::from_f32(acc.z * inv);
+    dst[3] = Conv<T>::from_f32(acc.w * inv);
+  }
+}
+
 // Result of partition `part` of the partition kernels.  A
 // sequence whose whole length fits in partition 0 needs no merge: its result
 // also goes straight to `out` (the merge kernel skips it), while the
@@ -106,6 +214,14 @@ __device__ __forceinline__ void write_partition_result(const DecodeParams& p, fl
                                                        int part, int seq_len, int tid, int nthreads, Sync sync) {
   const bool to_out = !p.split || (part == 0 && seq_len <= p.partition_size);
   write_merged_result<T, D, WARPS>(p, red, seq, kv_head, part, p.split != 0, to_out, tid, nthreads, sync);
+  if (p.merge_counters != nullptr && !to_out)
+    merge_if_last<T, D>(p, seq, kv_head, (seq_len + p.partition_size - 1) / p.partition_size, tid, nthreads, sync);
+}
+
+// Empty sequences get exact zeros from the partition kernel when no merge
+// kernel runs after it (single pass, or the single-launch merge).
+__device__ __forceinline__ bool partition_writes_zeros(const DecodeParams& p, int part, int seq_len) {
+  return !p.split || (p.merge_counters != nullptr && part == 0 && seq_len <= 0);
 }
 
 // Zeros for the group's query heads of an empty sequence (single-pass path),

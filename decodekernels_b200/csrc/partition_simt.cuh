@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
   const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
   const int pstart = part * p.partition_size;
   if (pstart >= seq_len) {
-    if (!p.split) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, kSimtThreads);
+    if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, kSimtThreads);
     pdl_launch_dependents();
     return;
   }

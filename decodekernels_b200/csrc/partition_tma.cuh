@@ -115,7 +115,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   if (pstart >= seq_len) {
     // Empty sequence (single pass writes zeros) or a partition past the end
     // (skipped; the merge kernel reads only live partitions).
-    if (!p.split) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
+    if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
     pdl_launch_dependents();
     return;
   }

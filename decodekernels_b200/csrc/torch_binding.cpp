@@ -43,10 +43,9 @@ std::string workspace_problem(const at::Tensor& tmp_out, const at::Tensor& max_l
   return "";
 }
 
-void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
-                            const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
-                            double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
-                            at::Tensor& exp_sums) {
+void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                 const at::Tensor& block_tables, const at::Tensor& seq_lens, double scale, int64_t max_seq_len,
+                 at::Tensor& tmp_out, at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor* merge_counters) {
   TORCH_CHECK(q.is_cuda(), "paged_attention_decode: q must be a CUDA tensor");
   TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "q and out must be [num_seqs, num_q_heads, head_dim]");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4,
@@ -102,6 +101,14 @@ void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tens
       max_partitions = static_cast<int32_t>(tmp_out.size(2));
     }
   }
+  int32_t* counters = nullptr;
+  if (merge_counters != nullptr && max_partitions > 0) {
+    const at::Tensor& c = *merge_counters;
+    TORCH_CHECK(c.scalar_type() == at::kInt && c.is_contiguous() && c.numel() >= num_seqs * num_kv_heads,
+                "merge_counters must be a contiguous int32 tensor of at least num_seqs * num_kv_heads elements");
+    TORCH_CHECK(c.device() == q.device(), "merge_counters must be on q's device");
+    counters = c.data_ptr<int32_t>();
+  }
   if (num_seqs == 0) return;
 
   DkPagedAttnArgs a{};
@@ -114,6 +121,7 @@ void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tens
   a.tmp_out = max_partitions ? tmp_out.data_ptr<float>() : nullptr;
   a.max_logits = max_partitions ? max_logits.data_ptr<float>() : nullptr;
   a.exp_sums = max_partitions ? exp_sums.data_ptr<float>() : nullptr;
+  a.merge_counters = counters;
   a.q_stride_seq = q.stride(0);
   a.q_stride_head = q.stride(1);
   a.out_stride_seq = out.stride(0);
@@ -144,12 +152,38 @@ void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tens
   TORCH_CHECK(status == 0, "paged_attention_decode failed: ", dk_last_error());
 }
 
+void paged_attention_decode(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                            const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                            double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
+                            at::Tensor& exp_sums) {
+  decode_impl(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+              nullptr);
+}
+
+// Same op with merge counters (int32 [num_seqs * num_kv_heads], zero before
+// the first call, left zero by every completed call): when the call splits,
+// the last partition of each (sequence, KV head) merges, so one kernel runs.
+void paged_attention_decode_fused(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                                  const at::Tensor& v_cache, const at::Tensor& block_tables,
+                                  const at::Tensor& seq_lens, double scale, int64_t max_seq_len, at::Tensor& tmp_out,
+                                  at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor& merge_counters) {
+  decode_impl(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+              &merge_counters);
+}
+
 }  // namespace
 
 TORCH_LIBRARY(decode_kernels, m) {
   m.def(
       "paged_attention_decode(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
       "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums) -> ()");
+  m.def(
+      "paged_attention_decode_fused(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
+      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
+      "Tensor! merge_counters) -> ()");
 }
 
-TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) { m.impl("paged_attention_decode", &paged_attention_decode); }
+TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) {
+  m.impl("paged_attention_decode", &paged_attention_decode);
+  m.impl("paged_attention_decode_fused", &paged_attention_decode_fused);
+}

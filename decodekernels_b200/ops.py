@@ -16,6 +16,10 @@ Differences that stay within the reference's contract:
   head count.
 * A non-empty workspace is also used when ``max_seq_len <= 512`` (small
   batches split to fill the GPU).
+* A 4-tuple workspace ``(tmp_out, max_logits, exp_sums, merge_counters)``
+  (``alloc_workspace(..., merge_counters=True)``) goes through
+  ``decode_kernels::paged_attention_decode_fused``, which may merge the
+  partitions inside the partition kernel (one launch instead of two).
 
 The native library is loaded from ``decodekernels_b200/lib``.  If it is not
 built, ``is_available()`` is False and every op raises; there is no CPU
@@ -37,11 +41,25 @@ SUPPORTED_HEAD_DIMS = (64, 128, 256)
 
 TORCH_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdk_b200_torch.so"
 
+def _register_fakes() -> None:
+    """Fake (meta) implementations let torch.compile trace through the ops."""
+
+    @torch.library.register_fake("decode_kernels::paged_attention_decode")
+    def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums):
+        return None
+
+    @torch.library.register_fake("decode_kernels::paged_attention_decode_fused")
+    def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+          merge_counters):
+        return None
+
+
 try:
     if not TORCH_LIB_PATH.exists():
         raise ImportError(f"{TORCH_LIB_PATH} is not built")
-    torch.ops.load_library(str(TORCH_LIB_PATH))  # registers torch.ops.decode_kernels.paged_attention_decode
+    torch.ops.load_library(str(TORCH_LIB_PATH))  # registers torch.ops.decode_kernels.paged_attention_decode{,_fused}
     capi.load()
+    _register_fakes()
     _AVAILABLE = True
     _IMPORT_ERROR: Exception | None = None
 except Exception as e:  # native library missing or stale: every op raises, nothing falls back
@@ -62,13 +80,6 @@ def _require() -> None:
         )
 
 
-if _AVAILABLE:
-    # Fake (meta) implementation lets torch.compile trace through the op.
-    @torch.library.register_fake("decode_kernels::paged_attention_decode")
-    def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums):
-        return None
-
-
 def num_partitions(max_seq_len: int) -> int:
     """Partitions of the reference's fixed 512-token split (ops.py:67-68)."""
     return max(1, math.ceil(max_seq_len / PARTITION_SIZE))
@@ -82,13 +93,19 @@ def _device_index(device) -> int:
 
 
 def alloc_workspace(num_seqs: int, num_q_heads: int, head_dim: int, max_seq_len: int, device, *,
-                    num_kv_heads: int | None = None, block_size: int = 16) -> tuple:
+                    num_kv_heads: int | None = None, block_size: int = 16, merge_counters: bool = False) -> tuple:
     """Split-K buffers ``(tmp_out, max_logits, exp_sums)`` for a call with these
     sizes, or three empty tensors when the call will run single-pass.
 
     Shapes: ``tmp_out [num_seqs, num_q_heads, P, head_dim]``, the other two
     ``[num_seqs, num_q_heads, P]``, float32, with ``P`` the planner's partition
     count (at least the reference's ``ceil(max_seq_len / 512)``).
+
+    ``merge_counters=True`` (needs ``num_kv_heads``) appends a zeroed int32
+    ``[num_seqs * num_kv_heads]`` tensor: calls given this 4-tuple merge the
+    partitions inside the partition kernel (one launch instead of two).  The
+    counters return to zero after every completed call; calls that may run
+    concurrently need separate workspaces.
     """
     _require()
     try:
@@ -103,6 +120,10 @@ def alloc_workspace(num_seqs: int, num_q_heads: int, head_dim: int, max_seq_len:
     tmp_out = torch.empty(num_seqs, num_q_heads, parts, head_dim, dtype=torch.float32, device=device)
     max_logits = torch.empty(num_seqs, num_q_heads, parts, dtype=torch.float32, device=device)
     exp_sums = torch.empty_like(max_logits)
+    if merge_counters:
+        if not num_kv_heads:
+            raise ValueError("merge_counters=True needs num_kv_heads")
+        return tmp_out, max_logits, exp_sums, torch.zeros(num_seqs * num_kv_heads, dtype=torch.int32, device=device)
     return tmp_out, max_logits, exp_sums
 
 
@@ -138,8 +159,15 @@ def paged_attention_decode(
         bs = k_cache.shape[1] if k_cache.dim() == 4 else 16
         workspace = alloc_workspace(num_seqs, num_q_heads, head_dim, max_seq_len, q.device, num_kv_heads=kv_heads,
                                     block_size=bs)
-    tmp_out, max_logits, exp_sums = workspace
-    torch.ops.decode_kernels.paged_attention_decode(
-        out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits, exp_sums
-    )
+    tmp_out, max_logits, exp_sums = workspace[:3]
+    if len(workspace) > 3 and workspace[3] is not None:
+        torch.ops.decode_kernels.paged_attention_decode_fused(
+            out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits,
+            exp_sums, workspace[3]
+        )
+    else:
+        torch.ops.decode_kernels.paged_attention_decode(
+            out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits,
+            exp_sums
+        )
     return out

@@ -55,7 +55,8 @@ enum {
 
 /* Bits of DkPagedAttnArgs.flags. */
 enum {
-  DK_FLAG_FORCE_SIMT = 1 /* take the CUDA-core path even when the TMA path is eligible (testing) */
+  DK_FLAG_FORCE_SIMT = 1,        /* take the CUDA-core path even when the TMA path is eligible (testing) */
+  DK_FLAG_FORCE_FUSED_MERGE = 2  /* with merge counters, merge in the partition kernel whatever the merge size */
 };
 
 /* Limits shared with the Python wrapper. */
@@ -80,6 +81,15 @@ enum {
  * partition p: its normalised partial output, its max scaled logit and its
  * exp-sum.  Set the three pointers to NULL and max_partitions to 0 when there
  * is no workspace; the call then runs single-pass.
+ * Optional merge counters (no counterpart in the reference): int32
+ * [num_seqs * num_kv_heads], all zero before the first call that uses them.
+ * When given, the plan splits and a (sequence, KV head)'s partition rows are
+ * small (<= 64 KB; any size with DK_FLAG_FORCE_FUSED_MERGE), the last
+ * partition of each pair to finish merges that pair's partitions itself, so
+ * the call is one kernel launch instead of two (DkPlan.launches says which).
+ * Every call that completes leaves the counters zero again.  Calls that can
+ * run concurrently need separate counters.  NULL keeps the separate merge
+ * kernel.
  */
 typedef struct DkPagedAttnArgs {
   void* out;
@@ -91,6 +101,7 @@ typedef struct DkPagedAttnArgs {
   float* tmp_out;
   float* max_logits;
   float* exp_sums;
+  int32_t* merge_counters; /* NULL, or num_seqs * num_kv_heads zeroed int32 (single-launch merge) */
   int64_t q_stride_seq, q_stride_head;
   int64_t out_stride_seq, out_stride_head;
   int64_t k_stride_block, k_stride_token, k_stride_head;
@@ -115,7 +126,7 @@ typedef struct DkPlan {
   int32_t num_ctas;       /* partition-kernel CTAs launched (including ones that exit early) */
   int32_t stages;         /* shared-memory pipeline depth of the TMA path */
   int32_t smem_bytes;     /* dynamic shared memory of the partition kernel */
-  int32_t launches;       /* kernels launched by one call (1 or 2) */
+  int32_t launches;       /* kernels launched by one call (1 or 2; 1 with merge counters) */
 } DkPlan;
 
 /*

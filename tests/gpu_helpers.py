@@ -23,8 +23,10 @@ def alloc_ws(num_seqs, num_q_heads, head_dim, parts, device, fill=float("nan")):
     return tmp, ml, es
 
 
-def run_capi(q, kv, scale=None, max_seq_len=None, partition_size=0, force_simt=False, workspace="auto", out=None):
-    """Call dk_paged_attention_decode; returns (out, workspace, plan)."""
+def run_capi(q, kv, scale=None, max_seq_len=None, partition_size=0, force_simt=False, workspace="auto", out=None,
+             counters=False, flags=0):
+    """Call dk_paged_attention_decode; returns (out, workspace, plan).  With
+    ``counters`` the workspace gets zeroed merge counters (single launch)."""
     n, hq, d = q.shape
     scale = d**-0.5 if scale is None else scale
     if max_seq_len is None:
@@ -37,10 +39,12 @@ def run_capi(q, kv, scale=None, max_seq_len=None, partition_size=0, force_simt=F
         else:
             parts = capi.num_partitions(n, kv.k_cache.shape[2], d, kv.k_cache.shape[1], max_seq_len)
         workspace = alloc_ws(n, hq, d, parts, q.device)
+        if counters:
+            workspace = (*workspace, torch.zeros(n * kv.k_cache.shape[2], dtype=torch.int32, device=q.device))
     plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, scale, max_seq_len, out, workspace,
-                     partition_size, force_simt)
+                     partition_size, force_simt, flags)
     capi.decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, scale, max_seq_len, out, workspace,
-                partition_size, force_simt)
+                partition_size, force_simt, flags=flags)
     torch.cuda.synchronize()
     return out, workspace, plan
 

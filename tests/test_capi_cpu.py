@@ -32,13 +32,32 @@ def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (dk_\w+)", out))
     assert set(_declared()) <= exported
-    assert capi.version() == 100
+    assert capi.version() == 200
 
 
-def test_struct_layout_matches_header():
-    # 9 pointers + 11 int64 + 11 int32 + 1 float = 208 bytes, no padding surprises
-    assert ctypes.sizeof(capi.DkPagedAttnArgs) == 208
+def test_struct_layout_matches_header(tmp_path):
+    """The ctypes mirrors have the C compiler's size and field offsets for
+    include/dk_paged_attention.h."""
+    # 10 pointers + 11 int64 + 11 int32 + 1 float = 216 bytes, no padding surprises
+    assert ctypes.sizeof(capi.DkPagedAttnArgs) == 216
     assert ctypes.sizeof(capi.DkPlan) == 32
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dk_paged_attention.h"', "int main(void) {"]
+    for struct, cls in (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan)):
+        lines.append(f'  printf("{struct} sizeof %zu\\n", sizeof({struct}));')
+        for name, _ in cls._fields_:
+            lines.append(f'  printf("{struct} {name} %zu\\n", offsetof({struct}, {name}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    include = Path(__file__).resolve().parents[1] / "include"
+    subprocess.run(["gcc", "-std=c99", "-I", str(include), str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                               check=True).stdout.splitlines())
+    for struct, cls in (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan)):
+        assert int(got[f"{struct} sizeof"]) == ctypes.sizeof(cls)
+        for name, _ in cls._fields_:
+            assert int(got[f"{struct} {name}"]) == getattr(cls, name).offset, (struct, name)
 
 
 def _args(**over):
@@ -128,6 +147,31 @@ def test_plan_respects_a_small_workspace():
     # a smaller workspace grows the partitions instead
     rc, p = _plan(_args(n=1, hq=64, hkv=8, max_seq_len=131072, ws=_ws(1, 64, 10)))
     assert rc == 0 and p["num_partitions"] <= 10 and p["partition_size"] % 64 == 0
+
+
+def test_plan_with_merge_counters_is_one_launch():
+    ctr = torch.zeros(4 * 8, dtype=torch.int32)
+    # 6 rows x 4 heads x 130 floats per (sequence, KV head): merged in the partition kernel
+    rc, p = _plan(_args(max_seq_len=3000, ws=(*_ws(4, 32, 47), ctr), partition_size=512))
+    assert rc == 0 and p["split"] == 1 and p["launches"] == 1
+    # 47 rows (97 KB): the separate merge kernel, unless forced
+    rc, p = _plan(_args(max_seq_len=3000, ws=(*_ws(4, 32, 47), ctr), partition_size=64))
+    assert rc == 0 and p["split"] == 1 and p["launches"] == 2
+    rc, p = _plan(_args(max_seq_len=3000, ws=(*_ws(4, 32, 47), ctr), partition_size=64,
+                        flags=capi.DK_FLAG_FORCE_FUSED_MERGE))
+    assert rc == 0 and p["split"] == 1 and p["launches"] == 1
+    # single pass ignores the counters
+    rc, p = _plan(_args(max_seq_len=3000, ws=None, merge_counters=ctr.data_ptr()))
+    assert rc == 0 and p["split"] == 0 and p["launches"] == 1
+    a = _args(max_seq_len=3000, ws=_ws(4, 32, 47))
+    a.merge_counters = ctr.data_ptr() + 2
+    assert _plan(a)[0] == 1 and "merge_counters" in capi.last_error()
+
+
+def test_misaligned_workspace_is_rejected():
+    a = _args(max_seq_len=3000, ws=_ws(4, 32, 47))
+    a.tmp_out += 4
+    assert _plan(a)[0] == 1 and "16-byte aligned" in capi.last_error()
 
 
 def test_plan_fixed_partition_size():
