@@ -5,6 +5,7 @@ A from-scratch, B200-native implementation of DecodeKernels'
 
     import decodekernels_b200 as dk
     out = dk.paged_attention_decode(q, k_cache, v_cache, block_tables, seq_lens)
+    dk.reshape_and_cache(key, value, k_cache, v_cache, slot_mapping)   # the paged-KV write before it
 
 The kernels live in ``libdk_b200.so`` (C ABI: ``include/dk_paged_attention.h``);
 ``torch.ops.decode_kernels.paged_attention_decode`` is registered by
@@ -19,6 +20,7 @@ from .ops import (
     is_available,
     num_partitions,
     paged_attention_decode,
+    reshape_and_cache,
 )
 
 __all__ = [
@@ -29,5 +31,6 @@ __all__ = [
     "is_available",
     "num_partitions",
     "paged_attention_decode",
+    "reshape_and_cache",
 ]
-__version__ = "0.1.0"
+__version__ = "0.3.0"

@@ -20,6 +20,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdk_b200.so"
 
 DK_DTYPE_FLOAT16 = 0
 DK_DTYPE_BFLOAT16 = 1
+DK_DTYPE_FP8_E4M3 = 2
 DK_PATH_NONE, DK_PATH_TMA_MMA, DK_PATH_SIMT = 0, 1, 2
 DK_FLAG_FORCE_SIMT = 1
 DK_FLAG_FORCE_FUSED_MERGE = 2
@@ -30,7 +31,7 @@ DK_REF_PARTITION_SIZE = 512
 DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
-            "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc")
+            "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -68,6 +69,35 @@ class DkPagedAttnArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("scale", ctypes.c_float),
+    ]
+
+
+class DkCacheWriteArgs(ctypes.Structure):
+    _fields_ = [
+        ("key", ctypes.c_void_p),
+        ("value", ctypes.c_void_p),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("slot_mapping", ctypes.c_void_p),
+        ("key_stride_token", ctypes.c_int64),
+        ("key_stride_head", ctypes.c_int64),
+        ("value_stride_token", ctypes.c_int64),
+        ("value_stride_head", ctypes.c_int64),
+        ("k_stride_block", ctypes.c_int64),
+        ("k_stride_token", ctypes.c_int64),
+        ("k_stride_head", ctypes.c_int64),
+        ("v_stride_block", ctypes.c_int64),
+        ("v_stride_token", ctypes.c_int64),
+        ("v_stride_head", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("num_blocks", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("cache_dtype", ctypes.c_int32),
+        ("k_scale", ctypes.c_float),
+        ("v_scale", ctypes.c_float),
     ]
 
 
@@ -114,6 +144,8 @@ def load() -> ctypes.CDLL:
         lib.dk_device_wait_timeouts.restype = ctypes.c_int
         lib.dk_version.argtypes = []
         lib.dk_version.restype = ctypes.c_int32
+        lib.dk_reshape_and_cache.argtypes = [ctypes.POINTER(DkCacheWriteArgs), ctypes.c_void_p]
+        lib.dk_reshape_and_cache.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -229,4 +261,45 @@ def decode_noalloc(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_l
     rc = load().dk_paged_attention_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_paged_attention_decode_noalloc failed ({rc}): {last_error()}")
+    return rc
+
+
+def _cache_dtype_code(t) -> int:
+    import torch
+
+    if t.dtype in (torch.uint8, torch.float8_e4m3fn):
+        return DK_DTYPE_FP8_E4M3
+    return _dtype_code(t)
+
+
+def make_cache_write_args(key, value, key_cache, value_cache, slot_mapping, k_scale: float = 1.0,
+                          v_scale: float = 1.0) -> DkCacheWriteArgs:
+    """Fill the paged-KV write struct from tensors (pointers + element strides)."""
+    a = DkCacheWriteArgs()
+    a.key, a.value = key.data_ptr(), value.data_ptr()
+    a.key_cache, a.value_cache = key_cache.data_ptr(), value_cache.data_ptr()
+    a.slot_mapping = slot_mapping.data_ptr()
+    a.key_stride_token, a.key_stride_head = key.stride(0), key.stride(1)
+    a.value_stride_token, a.value_stride_head = value.stride(0), value.stride(1)
+    a.k_stride_block, a.k_stride_token, a.k_stride_head = key_cache.stride()[:3]
+    a.v_stride_block, a.v_stride_token, a.v_stride_head = value_cache.stride()[:3]
+    a.num_tokens, a.num_kv_heads, a.head_dim = key.shape
+    a.num_blocks, a.block_size = key_cache.shape[0], key_cache.shape[1]
+    a.dtype = _dtype_code(key)
+    a.cache_dtype = _cache_dtype_code(key_cache)
+    a.k_scale, a.v_scale = float(k_scale), float(v_scale)
+    return a
+
+
+def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, k_scale: float = 1.0, v_scale: float = 1.0,
+                      stream=None) -> int:
+    """dk_reshape_and_cache on ``stream`` (default: torch's current stream)."""
+    import torch
+
+    a = make_cache_write_args(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale)
+    if stream is None:
+        stream = torch.cuda.current_stream(key.device).cuda_stream if key.is_cuda else 0
+    rc = load().dk_reshape_and_cache(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_reshape_and_cache failed ({rc}): {last_error()}")
     return rc

@@ -23,11 +23,12 @@
 #include "merge_partitions.cuh"
 #include "partition_simt.cuh"
 #include "partition_tma.cuh"
+#include "reshape_and_cache.cuh"
 
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 200;  // 0.2.0: DkPagedAttnArgs.merge_counters
+constexpr int kVersion = 300;  // 0.3.0: dk_reshape_and_cache (0.2.0: DkPagedAttnArgs.merge_counters)
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
 // at least kMinPartition tokens (overridable for tuning sweeps).
@@ -556,6 +557,83 @@ int noalloc_scratch(int dev, float** out, int** counters) {
   return 0;
 }
 
+// ---------------------------------------------------------------------------
+// Paged-KV write
+// ---------------------------------------------------------------------------
+int validate_cache_write(const DkCacheWriteArgs* a) {
+  if (a == nullptr) return fail(1, "dk_reshape_and_cache: args is NULL");
+  if (a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
+    return fail(1, "reshape_and_cache: key/value must be float16 or bfloat16 (dtype code %d)", a->dtype);
+  if (a->cache_dtype != a->dtype && a->cache_dtype != DK_DTYPE_FP8_E4M3)
+    return fail(1, "reshape_and_cache: cache dtype must match key/value or be fp8 e4m3 (code %d)", a->cache_dtype);
+  if (a->num_tokens < 0) return fail(1, "reshape_and_cache: num_tokens must be non-negative");
+  if (a->num_kv_heads <= 0 || a->head_dim <= 0 || a->block_size <= 0 || a->num_blocks <= 0)
+    return fail(1, "reshape_and_cache: num_kv_heads, head_dim, block_size and num_blocks must be positive");
+  if (a->cache_dtype == DK_DTYPE_FP8_E4M3 &&
+      !(a->k_scale > 0.0f && a->v_scale > 0.0f && a->k_scale < INFINITY && a->v_scale < INFINITY))
+    return fail(1, "reshape_and_cache: fp8 scales must be positive and finite");
+  if (a->num_tokens == 0) return 0;
+  if (!a->key || !a->value || !a->key_cache || !a->value_cache || !a->slot_mapping)
+    return fail(1, "reshape_and_cache: NULL tensor pointer");
+  const int64_t strides[10] = {a->key_stride_token, a->key_stride_head, a->value_stride_token, a->value_stride_head,
+                               a->k_stride_block,   a->k_stride_token,  a->k_stride_head,      a->v_stride_block,
+                               a->v_stride_token,   a->v_stride_head};
+  for (int64_t st : strides) {
+    if (st < 0) return fail(1, "reshape_and_cache: negative stride");
+  }
+  return 0;
+}
+
+template <typename T>
+int launch_cache_write(const DkCacheWriteArgs& a, cudaStream_t stream) {
+  CacheWriteParams p;
+  p.key = a.key;
+  p.value = a.value;
+  p.key_cache = a.key_cache;
+  p.value_cache = a.value_cache;
+  p.slot_mapping = a.slot_mapping;
+  p.key_stride_token = a.key_stride_token;
+  p.key_stride_head = a.key_stride_head;
+  p.value_stride_token = a.value_stride_token;
+  p.value_stride_head = a.value_stride_head;
+  p.k_stride_block = a.k_stride_block;
+  p.k_stride_token = a.k_stride_token;
+  p.k_stride_head = a.k_stride_head;
+  p.v_stride_block = a.v_stride_block;
+  p.v_stride_token = a.v_stride_token;
+  p.v_stride_head = a.v_stride_head;
+  p.num_slots = static_cast<int64_t>(a.num_blocks) * a.block_size;
+  p.num_kv_heads = a.num_kv_heads;
+  p.head_dim = a.head_dim;
+  p.block_size = a.block_size;
+  p.k_scale = a.k_scale;
+  p.v_scale = a.v_scale;
+  const bool fp8 = a.cache_dtype == DK_DTYPE_FP8_E4M3;
+  // 8-element steps when every row start is aligned for them
+  const size_t cache_esz = fp8 ? 1 : 2;
+  bool vec = a.head_dim % 8 == 0 && aligned(a.key, 16) && aligned(a.value, 16) &&
+             aligned(a.key_cache, 8 * cache_esz) && aligned(a.value_cache, 8 * cache_esz);
+  const int64_t strides[10] = {a.key_stride_token, a.key_stride_head, a.value_stride_token, a.value_stride_head,
+                               a.k_stride_block,   a.k_stride_token,  a.k_stride_head,      a.v_stride_block,
+                               a.v_stride_token,   a.v_stride_head};
+  for (int64_t st : strides) vec = vec && st % 8 == 0;
+  const dim3 grid(static_cast<unsigned>(a.num_tokens));
+  const dim3 block(kCacheWriteThreads);
+  if (fp8) {
+    if (vec)
+      reshape_and_cache_kernel<T, true, 8><<<grid, block, 0, stream>>>(p);
+    else
+      reshape_and_cache_kernel<T, true, 1><<<grid, block, 0, stream>>>(p);
+  } else {
+    if (vec)
+      reshape_and_cache_kernel<T, false, 8><<<grid, block, 0, stream>>>(p);
+    else
+      reshape_and_cache_kernel<T, false, 1><<<grid, block, 0, stream>>>(p);
+  }
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail_cuda(e, "reshape_and_cache kernel launch");
+}
+
 }  // namespace
 }  // namespace dkb
 
@@ -646,6 +724,14 @@ int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_d
   const int hkv = num_kv_heads <= 0 ? 1 : num_kv_heads;
   const int ps = dkb::desired_partition_size(num_seqs, hkv, head_dim, max_seq_len, dkb::num_sms(dev));
   return dkb::ceil_div(max_seq_len, ps);
+}
+
+int dk_reshape_and_cache(const DkCacheWriteArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate_cache_write(args)) return e;
+  if (args->num_tokens == 0) return 0;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return args->dtype == DK_DTYPE_BFLOAT16 ? dkb::launch_cache_write<__nv_bfloat16>(*args, s)
+                                          : dkb::launch_cache_write<__half>(*args, s);
 }
 
 const char* dk_last_error(void) { return dkb::g_last_error; }

@@ -171,6 +171,65 @@ void paged_attention_decode_fused(at::Tensor& out, const at::Tensor& q, const at
               &merge_counters);
 }
 
+// Paged-KV write (dk_reshape_and_cache): key/value [T, Hkv, D] into caches
+// [blocks, bs, Hkv, D] (any strides on the first three dims) at slot_mapping
+// (int64; negative = padding).  A uint8 / float8_e4m3fn cache stores
+// sat_e4m3(x / scale).
+void reshape_and_cache(const at::Tensor& key, const at::Tensor& value, at::Tensor& key_cache, at::Tensor& value_cache,
+                       const at::Tensor& slot_mapping, double k_scale, double v_scale) {
+  TORCH_CHECK(key.is_cuda(), "reshape_and_cache: key must be a CUDA tensor");
+  TORCH_CHECK(key.dim() == 3 && value.sizes() == key.sizes(), "key and value must be [num_tokens, num_kv_heads, head_dim]");
+  TORCH_CHECK(key_cache.dim() == 4 && value_cache.sizes() == key_cache.sizes(),
+              "key_cache and value_cache must be [num_blocks, block_size, num_kv_heads, head_dim]");
+  TORCH_CHECK(key_cache.size(2) == key.size(1) && key_cache.size(3) == key.size(2),
+              "cache heads / head_dim do not match key");
+  check_same(key, value, "key/value");
+  TORCH_CHECK(key_cache.scalar_type() == value_cache.scalar_type(), "key_cache/value_cache: dtype mismatch");
+  TORCH_CHECK(key.device() == key_cache.device() && key.device() == value_cache.device() &&
+                  key.device() == slot_mapping.device(),
+              "reshape_and_cache: tensors must be on the same device");
+  TORCH_CHECK(key.scalar_type() == at::kHalf || key.scalar_type() == at::kBFloat16,
+              "reshape_and_cache: key/value must be float16 or bfloat16, got ", key.scalar_type());
+  const bool fp8 = key_cache.scalar_type() == at::kByte || key_cache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(fp8 || key_cache.scalar_type() == key.scalar_type(),
+              "reshape_and_cache: cache must have key's dtype or be uint8 / float8_e4m3fn (fp8 e4m3)");
+  TORCH_CHECK(key.stride(2) == 1 && value.stride(2) == 1 && key_cache.stride(3) == 1 && value_cache.stride(3) == 1,
+              "head_dim must be the contiguous (innermost) dimension");
+  TORCH_CHECK(slot_mapping.scalar_type() == at::kLong && slot_mapping.dim() == 1 && slot_mapping.is_contiguous() &&
+                  slot_mapping.size(0) >= key.size(0),
+              "slot_mapping must be a contiguous int64 tensor with at least num_tokens entries");
+  TORCH_CHECK(key.size(0) <= INT32_MAX && key_cache.size(0) <= INT32_MAX, "reshape_and_cache: sizes out of range");
+  DkCacheWriteArgs a{};
+  a.key = key.data_ptr();
+  a.value = value.data_ptr();
+  a.key_cache = key_cache.data_ptr();
+  a.value_cache = value_cache.data_ptr();
+  a.slot_mapping = slot_mapping.data_ptr<int64_t>();
+  a.key_stride_token = key.stride(0);
+  a.key_stride_head = key.stride(1);
+  a.value_stride_token = value.stride(0);
+  a.value_stride_head = value.stride(1);
+  a.k_stride_block = key_cache.stride(0);
+  a.k_stride_token = key_cache.stride(1);
+  a.k_stride_head = key_cache.stride(2);
+  a.v_stride_block = value_cache.stride(0);
+  a.v_stride_token = value_cache.stride(1);
+  a.v_stride_head = value_cache.stride(2);
+  a.num_tokens = static_cast<int32_t>(key.size(0));
+  a.num_kv_heads = static_cast<int32_t>(key.size(1));
+  a.head_dim = static_cast<int32_t>(key.size(2));
+  a.block_size = static_cast<int32_t>(key_cache.size(1));
+  a.num_blocks = static_cast<int32_t>(key_cache.size(0));
+  a.dtype = key.scalar_type() == at::kBFloat16 ? DK_DTYPE_BFLOAT16 : DK_DTYPE_FLOAT16;
+  a.cache_dtype = fp8 ? DK_DTYPE_FP8_E4M3 : a.dtype;
+  a.k_scale = static_cast<float>(k_scale);
+  a.v_scale = static_cast<float>(v_scale);
+  const c10::cuda::OptionalCUDAGuard guard(key.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(key.device().index()).stream();
+  const int status = dk_reshape_and_cache(&a, reinterpret_cast<dk_stream_t>(stream));
+  TORCH_CHECK(status == 0, "reshape_and_cache failed: ", dk_last_error());
+}
+
 }  // namespace
 
 TORCH_LIBRARY(decode_kernels, m) {
@@ -181,9 +240,13 @@ TORCH_LIBRARY(decode_kernels, m) {
       "paged_attention_decode_fused(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
       "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
       "Tensor! merge_counters) -> ()");
+  m.def(
+      "reshape_and_cache(Tensor key, Tensor value, Tensor! key_cache, Tensor! value_cache, Tensor slot_mapping, "
+      "float k_scale, float v_scale) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) {
   m.impl("paged_attention_decode", &paged_attention_decode);
   m.impl("paged_attention_decode_fused", &paged_attention_decode_fused);
+  m.impl("reshape_and_cache", &reshape_and_cache);
 }

@@ -53,6 +53,10 @@ def _register_fakes() -> None:
           merge_counters):
         return None
 
+    @torch.library.register_fake("decode_kernels::reshape_and_cache")
+    def _(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale):
+        return None
+
 
 try:
     if not TORCH_LIB_PATH.exists():
@@ -171,3 +175,18 @@ def paged_attention_decode(
             exp_sums
         )
     return out
+
+
+def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                      slot_mapping: torch.Tensor, k_scale: float = 1.0, v_scale: float = 1.0) -> None:
+    """Paged-KV write, the step before decode (vLLM's ``reshape_and_cache_flash``).
+
+    key / value: [num_tokens, num_kv_heads, head_dim] (fp16/bf16);
+    key_cache / value_cache: [num_blocks, block_size, num_kv_heads, head_dim]
+    in any of the decode's layouts, with key's dtype or uint8 /
+    float8_e4m3fn (stored as ``sat_e4m3(x / scale)``); slot_mapping: int64
+    [num_tokens], ``block * block_size + offset``, negative = padding.
+    """
+    _require()
+    torch.ops.decode_kernels.reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, float(k_scale),
+                                               float(v_scale))

@@ -43,8 +43,9 @@ extern "C" {
 /* Same object as cudaStream_t; declared here so the header needs no CUDA headers. */
 typedef struct CUstream_st* dk_stream_t;
 
-/* Element type of q, out and the K/V caches. */
-enum { DK_DTYPE_FLOAT16 = 0, DK_DTYPE_BFLOAT16 = 1 };
+/* Element types: q, out and the K/V caches of the decode; key / value and
+ * the caches of the paged-KV write (which may also store e4m3 bytes). */
+enum { DK_DTYPE_FLOAT16 = 0, DK_DTYPE_BFLOAT16 = 1, DK_DTYPE_FP8_E4M3 = 2 };
 
 /* Kernel paths reported by dk_plan. */
 enum {
@@ -172,6 +173,43 @@ DK_API int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan);
  */
 DK_API int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
                           int32_t max_seq_len, int32_t device);
+
+/*
+ * Paged-KV write, the step before decode: no counterpart in DecodeKernels
+ * (its decode reads caches that vLLM's reshape_and_cache_flash wrote); this
+ * is that operation.  For every token t with slot = slot_mapping[t] in
+ * [0, num_blocks * block_size):
+ *   key_cache[slot / block_size, slot % block_size, h, :] = key[t, h, :]
+ *   value_cache[...]                                      = value[t, h, :]
+ * Negative slots (padding) and slots past the cache are skipped.  With
+ * cache_dtype DK_DTYPE_FP8_E4M3 each element is stored as
+ * sat_e4m3(x / scale) (IEEE fp32 division, round-to-nearest-even, saturating
+ * to +-448, NaN kept), k_scale for keys and v_scale for values.  Shapes
+ * (strides in ELEMENTS, head_dim contiguous):
+ *   key, value          [num_tokens, num_kv_heads, head_dim]
+ *   key/value_cache     [num_blocks, block_size, num_kv_heads, head_dim], any
+ *                       strides on the first three dims (the decode's layouts)
+ *   slot_mapping        int64 [num_tokens], on the device
+ * Asynchronous on `stream`, no allocation; returns 0 or a cudaError_t code
+ * (1 for rejected arguments).
+ */
+typedef struct DkCacheWriteArgs {
+  const void* key;
+  const void* value;
+  void* key_cache;
+  void* value_cache;
+  const int64_t* slot_mapping;
+  int64_t key_stride_token, key_stride_head;
+  int64_t value_stride_token, value_stride_head;
+  int64_t k_stride_block, k_stride_token, k_stride_head;
+  int64_t v_stride_block, v_stride_token, v_stride_head;
+  int32_t num_tokens, num_kv_heads, head_dim, block_size, num_blocks;
+  int32_t dtype;       /* DK_DTYPE_FLOAT16 or DK_DTYPE_BFLOAT16: key and value */
+  int32_t cache_dtype; /* dtype, or DK_DTYPE_FP8_E4M3 */
+  float k_scale, v_scale; /* FP8 cache only: positive and finite */
+} DkCacheWriteArgs;
+
+DK_API int dk_reshape_and_cache(const DkCacheWriteArgs* args, dk_stream_t stream);
 
 /* Message describing the calling thread's last failed call ("" if none). */
 DK_API const char* dk_last_error(void);

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (dk_\w+)", out))
     assert set(_declared()) <= exported
-    assert capi.version() == 200
+    assert capi.version() == 300
 
 
 def test_struct_layout_matches_header(tmp_path):
@@ -42,7 +42,9 @@ def test_struct_layout_matches_header(tmp_path):
     assert ctypes.sizeof(capi.DkPagedAttnArgs) == 216
     assert ctypes.sizeof(capi.DkPlan) == 32
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dk_paged_attention.h"', "int main(void) {"]
-    for struct, cls in (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan)):
+    structs = (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan),
+               ("DkCacheWriteArgs", capi.DkCacheWriteArgs))
+    for struct, cls in structs:
         lines.append(f'  printf("{struct} sizeof %zu\\n", sizeof({struct}));')
         for name, _ in cls._fields_:
             lines.append(f'  printf("{struct} {name} %zu\\n", offsetof({struct}, {name}));')
@@ -54,7 +56,7 @@ def test_struct_layout_matches_header(tmp_path):
     subprocess.run(["gcc", "-std=c99", "-I", str(include), str(src), "-o", str(exe)], check=True)
     got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], capture_output=True, text=True,
                                                                check=True).stdout.splitlines())
-    for struct, cls in (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan)):
+    for struct, cls in structs:
         assert int(got[f"{struct} sizeof"]) == ctypes.sizeof(cls)
         for name, _ in cls._fields_:
             assert int(got[f"{struct} {name}"]) == getattr(cls, name).offset, (struct, name)
