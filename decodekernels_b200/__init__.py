@@ -18,8 +18,10 @@ from .ops import (
     SUPPORTED_HEAD_DIMS,
     alloc_workspace,
     is_available,
+    merge_lse,
     num_partitions,
     paged_attention_decode,
+    paged_attention_decode_lse,
     reshape_and_cache,
 )
 
@@ -29,8 +31,10 @@ __all__ = [
     "SUPPORTED_HEAD_DIMS",
     "alloc_workspace",
     "is_available",
+    "merge_lse",
     "num_partitions",
     "paged_attention_decode",
+    "paged_attention_decode_lse",
     "reshape_and_cache",
 ]
-__version__ = "0.3.0"
+__version__ = "0.4.0"

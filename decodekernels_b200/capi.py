@@ -31,7 +31,8 @@ DK_REF_PARTITION_SIZE = 512
 DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
-            "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache")
+            "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache",
+            "dk_paged_attention_decode_lse", "dk_merge_lse")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -101,6 +102,22 @@ class DkCacheWriteArgs(ctypes.Structure):
     ]
 
 
+class DkLseMergeArgs(ctypes.Structure):
+    _fields_ = [
+        ("parts", ctypes.c_void_p),
+        ("part_stride", ctypes.c_int64),
+        ("out", ctypes.c_void_p),
+        ("out_stride_seq", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("num_parts", ctypes.c_int32),
+        ("num_seqs", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("out_partial", ctypes.c_int32),
+    ]
+
+
 class DkPlan(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int32),
@@ -146,6 +163,11 @@ def load() -> ctypes.CDLL:
         lib.dk_version.restype = ctypes.c_int32
         lib.dk_reshape_and_cache.argtypes = [ctypes.POINTER(DkCacheWriteArgs), ctypes.c_void_p]
         lib.dk_reshape_and_cache.restype = ctypes.c_int
+        lib.dk_paged_attention_decode_lse.argtypes = [ctypes.POINTER(DkPagedAttnArgs), ctypes.c_void_p,
+                                                      ctypes.c_void_p]
+        lib.dk_paged_attention_decode_lse.restype = ctypes.c_int
+        lib.dk_merge_lse.argtypes = [ctypes.POINTER(DkLseMergeArgs), ctypes.c_void_p]
+        lib.dk_merge_lse.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -302,4 +324,47 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, k_scale:
     rc = load().dk_reshape_and_cache(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_reshape_and_cache failed ({rc}): {last_error()}")
+    return rc
+
+
+def decode_lse(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, partial, workspace=None,
+               partition_size: int = 0, stream=None, flags: int = 0) -> int:
+    """dk_paged_attention_decode_lse: fp32 rows (o, lse, pad) into ``partial`` [n, Hq, D + 4]."""
+    import torch
+
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, partial, workspace, partition_size,
+                  False, flags)
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
+    rc = load().dk_paged_attention_decode_lse(ctypes.byref(a), ctypes.c_void_p(partial.data_ptr()),
+                                              ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_paged_attention_decode_lse failed ({rc}): {last_error()}")
+    return rc
+
+
+def make_lse_merge_args(parts, out) -> DkLseMergeArgs:
+    """Struct for parts [R, n, Hq, D + 4] fp32 and out [n, Hq, D] (fp16 / bf16) or [n, Hq, D + 4] fp32."""
+    import torch
+
+    a = DkLseMergeArgs()
+    a.parts, a.part_stride = parts.data_ptr(), parts.stride(0)
+    a.out, a.out_stride_seq, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.num_parts, a.num_seqs, a.num_q_heads = parts.shape[0], parts.shape[1], parts.shape[2]
+    a.head_dim = parts.shape[3] - 4
+    a.out_partial = 1 if out.dtype == torch.float32 else 0
+    a.dtype = _dtype_code(out) if not a.out_partial else DK_DTYPE_FLOAT16
+    return a
+
+
+def merge_lse(parts, out, stream=None) -> int:
+    """dk_merge_lse on ``stream`` (default: torch's current stream)."""
+    import torch
+
+    a = make_lse_merge_args(parts, out)
+    if stream is None:
+        stream = torch.cuda.current_stream(parts.device).cuda_stream if parts.is_cuda else 0
+    rc = load().dk_merge_lse(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_merge_lse failed ({rc}): {last_error()}")
     return rc

@@ -45,6 +45,7 @@ struct DecodeParams {
   int ws_partitions;   // workspace row stride (capacity)
   int split;           // 1: partitions write the workspace and the merge kernel writes out
   int kv_fused;        // 1: one tensor map covers K and V (vLLM's interleaved K|V rows)
+  int lse_mode;        // 1: `out` is fp32 rows [o (head_dim) | lse | 3 pad] per (seq, q_head), not T
   float scale_log2;    // softmax scale * log2(e)
 };
 

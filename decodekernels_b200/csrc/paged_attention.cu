@@ -28,7 +28,8 @@
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 300;  // 0.3.0: dk_reshape_and_cache (0.2.0: DkPagedAttnArgs.merge_counters)
+constexpr int kVersion = 400;  // 0.4.0: dk_paged_attention_decode_lse / dk_merge_lse (0.3.0: dk_reshape_and_cache;
+                                // 0.2.0: DkPagedAttnArgs.merge_counters)
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
 // at least kMinPartition tokens (overridable for tuning sweeps).
@@ -469,9 +470,10 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
   return 0;
 }
 
-int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream) {
+int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream, bool lse_mode = false) {
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
+  p.lse_mode = lse_mode ? 1 : 0;
   p.out = a.out;
   p.q = a.q;
   p.k_cache = a.k_cache;
@@ -555,6 +557,47 @@ int noalloc_scratch(int dev, float** out, int** counters) {
   *out = g_noalloc_ptr[dev];
   *counters = g_noalloc_ctr[dev];
   return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Merge of partials over disjoint token ranges
+// ---------------------------------------------------------------------------
+int validate_lse_merge(const DkLseMergeArgs* a) {
+  if (a == nullptr) return fail(1, "dk_merge_lse: args is NULL");
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(1, "head_dim must be 64, 128 or 256, got %d", a->head_dim);
+  if (a->num_parts < 1 || a->num_seqs < 0 || a->num_q_heads <= 0)
+    return fail(1, "dk_merge_lse: num_parts must be >= 1, num_seqs >= 0, num_q_heads > 0");
+  if (!a->out_partial && a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
+    return fail(1, "dk_merge_lse: out must be float16 or bfloat16 (dtype code %d)", a->dtype);
+  const int64_t rows = static_cast<int64_t>(a->num_seqs) * a->num_q_heads * (a->head_dim + 4);
+  if (a->num_parts > 1 && a->part_stride < rows) return fail(1, "dk_merge_lse: part_stride overlaps the parts");
+  if (a->num_seqs == 0) return 0;
+  if (!a->parts || !a->out) return fail(1, "dk_merge_lse: NULL pointer");
+  if (a->out_stride_seq < 0 || a->out_stride_head < 0) return fail(1, "dk_merge_lse: negative stride");
+  return 0;
+}
+
+template <int D>
+int launch_lse_merge(const DkLseMergeArgs& a, cudaStream_t stream) {
+  LseMergeParams p;
+  p.parts = a.parts;
+  p.part_stride = a.part_stride;
+  p.out = a.out;
+  p.out_stride_seq = a.out_stride_seq;
+  p.out_stride_head = a.out_stride_head;
+  p.num_parts = a.num_parts;
+  p.num_seqs = a.num_seqs;
+  p.num_q_heads = a.num_q_heads;
+  p.out_lse = a.out_partial;
+  const long long pairs = static_cast<long long>(a.num_seqs) * a.num_q_heads;
+  const dim3 grid(static_cast<unsigned>((pairs + kLseMergeThreads / 32 - 1) / (kLseMergeThreads / 32)));
+  if (a.out_partial || a.dtype == DK_DTYPE_FLOAT16)
+    merge_lse_kernel<__half, D><<<grid, kLseMergeThreads, 0, stream>>>(p);
+  else
+    merge_lse_kernel<__nv_bfloat16, D><<<grid, kLseMergeThreads, 0, stream>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail_cuda(e, "LSE merge kernel launch");
 }
 
 // ---------------------------------------------------------------------------
@@ -724,6 +767,39 @@ int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_d
   const int hkv = num_kv_heads <= 0 ? 1 : num_kv_heads;
   const int ps = dkb::desired_partition_size(num_seqs, hkv, head_dim, max_seq_len, dkb::num_sms(dev));
   return dkb::ceil_div(max_seq_len, ps);
+}
+
+int dk_paged_attention_decode_lse(const DkPagedAttnArgs* args, float* partial, dk_stream_t stream) {
+  if (args == nullptr) return dkb::fail(1, "dk_paged_attention_decode_lse: args is NULL");
+  DkPagedAttnArgs a = *args;
+  a.out = partial;
+  a.out_stride_head = a.head_dim + 4;
+  a.out_stride_seq = static_cast<int64_t>(a.num_q_heads) * a.out_stride_head;
+  if (int e = dkb::validate(&a)) return e;
+  if (a.num_seqs == 0) return 0;
+  if (!dkb::aligned(partial, 16)) return dkb::fail(1, "dk_paged_attention_decode_lse: partial must be 16-byte aligned");
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  DkPlan pl;
+  dkb::make_plan(a, dev, &pl);
+  if (pl.split && a.max_partitions < pl.num_partitions)
+    return dkb::fail(1, "split-K workspace too small: %d partitions needed", pl.num_partitions);
+  return dkb::launch(a, pl, dev, reinterpret_cast<cudaStream_t>(stream), /*lse_mode=*/true);
+}
+
+int dk_merge_lse(const DkLseMergeArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate_lse_merge(args)) return e;
+  if (args->num_seqs == 0) return 0;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (args->head_dim) {
+    case 64:
+      return dkb::launch_lse_merge<64>(*args, s);
+    case 128:
+      return dkb::launch_lse_merge<128>(*args, s);
+    default:
+      return dkb::launch_lse_merge<256>(*args, s);
+  }
 }
 
 int dk_reshape_and_cache(const DkCacheWriteArgs* args, dk_stream_t stream) {

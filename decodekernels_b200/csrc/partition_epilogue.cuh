@@ -14,6 +14,25 @@
 
 namespace dkb {
 
+// Final result of (seq, q_head), columns d..d+3, already normalised.  In LSE
+// mode (p.lse_mode) `out` holds fp32 rows (o, lse, pad) and `lse2` -- the
+// log2-domain log-sum-exp of the scaled logits, -inf for an empty sequence --
+// is stored as a natural log by the thread that writes d == 0.
+template <typename T, int D>
+__device__ __forceinline__ void store_out4(const DecodeParams& p, int seq, int q_head, int d, float4 o, float lse2) {
+  if (p.lse_mode) {
+    float* row = static_cast<float*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head;
+    *reinterpret_cast<float4*>(row + d) = o;
+    if (d == 0) row[D] = lse2 * kLn2;
+    return;
+  }
+  T* dst = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head + d;
+  dst[0] = Conv<T>::from_f32(o.x);
+  dst[1] = Conv<T>::from_f32(o.y);
+  dst[2] = Conv<T>::from_f32(o.z);
+  dst[3] = Conv<T>::from_f32(o.w);
+}
+
 // Shared-memory scratch of the merge: per-warp output rows (row stride D + 4
 // keeps the fragment-ordered stores free of bank conflicts and the rows
 // 16-byte aligned), per-warp (m, l), then the per-(warp, head) merge factors
@@ -87,13 +106,7 @@ __device__ __forceinline__ void write_merged_result(const DecodeParams& p, float
         p.exp_sums[wrow] = head[kMaxGroup + h];
       }
     }
-    if (to_out) {
-      T* dst = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head + d;
-      dst[0] = Conv<T>::from_f32(o.x);
-      dst[1] = Conv<T>::from_f32(o.y);
-      dst[2] = Conv<T>::from_f32(o.z);
-      dst[3] = Conv<T>::from_f32(o.w);
-    }
+    if (to_out) store_out4<T, D>(p, seq, q_head, d, o, head[h] + __log2f(head[kMaxGroup + h]));
   }
 }
 
@@ -197,11 +210,8 @@ __device__ __forceinline__ void merge_if_last(const DecodeParams& p, int seq, in
       }
     }
     const float inv = sh[1 + kMaxGroup + h];
-    T* dst = static_cast<T*>(p.out) + seq * p.out_stride_seq + (kv_head * group + h) * p.out_stride_head + d;
-    dst[0] = Conv<T>::from_f32(acc.x * inv);
-    dst[1] = Conv<T>::from_f32(acc.y * inv);
-    dst[2] = Conv<T>::from_f32(acc.z * inv);
-    dst[3] = Conv<T>::from_f32(acc.w * inv);
+    store_out4<T, D>(p, seq, kv_head * group + h, d,
+                     make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv), m2 - __log2f(inv));
   }
 }
 
@@ -228,11 +238,10 @@ __device__ __forceinline__ bool partition_writes_zeros(const DecodeParams& p, in
 // matching csrc/paged_attention.cuh:91-105.
 template <typename T, int D>
 __device__ __forceinline__ void write_zero_output(const DecodeParams& p, int seq, int kv_head, int tid, int nthreads) {
-  for (int idx = tid; idx < p.group * D; idx += nthreads) {
-    const int h = idx / D;
-    const int d = idx - h * D;
-    const int q_head = kv_head * p.group + h;
-    static_cast<T*>(p.out)[seq * p.out_stride_seq + q_head * p.out_stride_head + d] = Conv<T>::from_f32(0.0f);
+  constexpr int Q = D / 4;
+  for (int idx = tid; idx < p.group * Q; idx += nthreads) {
+    const int h = idx / Q;
+    store_out4<T, D>(p, seq, kv_head * p.group + h, (idx - h * Q) * 4, make_float4(0.0f, 0.0f, 0.0f, 0.0f), -INFINITY);
   }
 }
 

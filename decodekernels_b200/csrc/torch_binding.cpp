@@ -43,17 +43,29 @@ std::string workspace_problem(const at::Tensor& tmp_out, const at::Tensor& max_l
   return "";
 }
 
+// `partial` non-null: results go to fp32 rows (o, lse, pad) [n, Hq, D + 4]
+// through dk_paged_attention_decode_lse and `out` is not used.
 void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                  const at::Tensor& block_tables, const at::Tensor& seq_lens, double scale, int64_t max_seq_len,
-                 at::Tensor& tmp_out, at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor* merge_counters) {
+                 at::Tensor& tmp_out, at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor* merge_counters,
+                 at::Tensor* partial = nullptr) {
   TORCH_CHECK(q.is_cuda(), "paged_attention_decode: q must be a CUDA tensor");
-  TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "q and out must be [num_seqs, num_q_heads, head_dim]");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4,
               "k_cache and v_cache must be [num_blocks, block_size, num_kv_heads, head_dim]");
-  check_same(q, out, "q/out");
+  if (partial == nullptr) {
+    TORCH_CHECK(q.dim() == 3 && out.dim() == 3, "q and out must be [num_seqs, num_q_heads, head_dim]");
+    check_same(q, out, "q/out");
+    TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
+  } else {
+    TORCH_CHECK(q.dim() == 3, "q must be [num_seqs, num_q_heads, head_dim]");
+    TORCH_CHECK(partial->scalar_type() == at::kFloat && partial->is_contiguous() && partial->dim() == 3 &&
+                    partial->size(0) == q.size(0) && partial->size(1) == q.size(1) &&
+                    partial->size(2) == q.size(2) + 4,
+                "partial must be a contiguous float32 [num_seqs, num_q_heads, head_dim + 4] tensor");
+    TORCH_CHECK(partial->device() == q.device(), "partial must be on q's device");
+  }
   check_same(q, k_cache, "q/k_cache");
   check_same(q, v_cache, "q/v_cache");
-  TORCH_CHECK(out.sizes() == q.sizes(), "out must have the same shape as q");
   TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache shapes differ");
   TORCH_CHECK(q.scalar_type() == at::kHalf || q.scalar_type() == at::kBFloat16,
               "paged_attention_decode: expected float16 or bfloat16, got ", q.scalar_type());
@@ -69,7 +81,8 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
   TORCH_CHECK(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "num_q_heads must be a multiple of num_kv_heads");
   TORCH_CHECK(num_q_heads / num_kv_heads <= DK_MAX_GQA_GROUP, "GQA group size above ", DK_MAX_GQA_GROUP,
               " is not supported");
-  TORCH_CHECK(q.stride(2) == 1 && out.stride(2) == 1 && k_cache.stride(3) == 1 && v_cache.stride(3) == 1,
+  TORCH_CHECK(q.stride(2) == 1 && (partial != nullptr || out.stride(2) == 1) && k_cache.stride(3) == 1 &&
+                  v_cache.stride(3) == 1,
               "head_dim must be the contiguous (innermost) dimension");
   const int64_t vec = head_dim / 32;
   for (int d = 0; d < 3; ++d) {
@@ -112,7 +125,7 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
   if (num_seqs == 0) return;
 
   DkPagedAttnArgs a{};
-  a.out = out.data_ptr();
+  a.out = partial == nullptr ? out.data_ptr() : nullptr;
   a.q = q.data_ptr();
   a.k_cache = k_cache.data_ptr();
   a.v_cache = v_cache.data_ptr();
@@ -124,8 +137,8 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
   a.merge_counters = counters;
   a.q_stride_seq = q.stride(0);
   a.q_stride_head = q.stride(1);
-  a.out_stride_seq = out.stride(0);
-  a.out_stride_head = out.stride(1);
+  a.out_stride_seq = partial == nullptr ? out.stride(0) : 0;
+  a.out_stride_head = partial == nullptr ? out.stride(1) : 0;
   a.k_stride_block = k_cache.stride(0);
   a.k_stride_token = k_cache.stride(1);
   a.k_stride_head = k_cache.stride(2);
@@ -148,7 +161,10 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
 
   const c10::cuda::OptionalCUDAGuard guard(q.device());
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  const int status = dk_paged_attention_decode(&a, reinterpret_cast<dk_stream_t>(stream));
+  const int status =
+      partial == nullptr
+          ? dk_paged_attention_decode(&a, reinterpret_cast<dk_stream_t>(stream))
+          : dk_paged_attention_decode_lse(&a, partial->data_ptr<float>(), reinterpret_cast<dk_stream_t>(stream));
   TORCH_CHECK(status == 0, "paged_attention_decode failed: ", dk_last_error());
 }
 
@@ -169,6 +185,51 @@ void paged_attention_decode_fused(at::Tensor& out, const at::Tensor& q, const at
                                   at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor& merge_counters) {
   decode_impl(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
               &merge_counters);
+}
+
+// Partials for sequence-sharded decode: fp32 rows (o, lse, pad).
+void paged_attention_decode_lse(at::Tensor& partial, const at::Tensor& q, const at::Tensor& k_cache,
+                                const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                                double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
+                                at::Tensor& exp_sums) {
+  at::Tensor unused;
+  decode_impl(unused, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+              nullptr, &partial);
+}
+
+// Merge partials [R, n, Hq, D + 4] (disjoint token ranges) into out: the
+// attention output [n, Hq, D] (fp16 / bf16, any head / seq strides) or fp32
+// partial rows [n, Hq, D + 4].
+void merge_lse(at::Tensor& out, const at::Tensor& parts) {
+  TORCH_CHECK(parts.is_cuda() && parts.scalar_type() == at::kFloat && parts.is_contiguous() && parts.dim() == 4,
+              "parts must be a contiguous CUDA float32 [num_parts, num_seqs, num_q_heads, head_dim + 4] tensor");
+  TORCH_CHECK(out.device() == parts.device(), "merge_lse: out and parts must be on the same device");
+  const int64_t D = parts.size(3) - 4;
+  TORCH_CHECK(out.dim() == 3 && out.size(0) == parts.size(1) && out.size(1) == parts.size(2),
+              "out must be [num_seqs, num_q_heads, head_dim] or [num_seqs, num_q_heads, head_dim + 4]");
+  const bool as_partial = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(as_partial ? (out.size(2) == D + 4 && out.is_contiguous())
+                         : (out.size(2) == D && out.stride(2) == 1 &&
+                            (out.scalar_type() == at::kHalf || out.scalar_type() == at::kBFloat16)),
+              "merge_lse: out must be float16 / bfloat16 [.., head_dim] or contiguous float32 [.., head_dim + 4]");
+  TORCH_CHECK(parts.size(0) <= INT32_MAX && parts.size(1) <= INT32_MAX && parts.size(2) <= INT32_MAX,
+              "merge_lse: sizes out of range");
+  DkLseMergeArgs a{};
+  a.parts = parts.data_ptr<float>();
+  a.part_stride = parts.stride(0);
+  a.out = out.data_ptr();
+  a.out_stride_seq = out.stride(0);
+  a.out_stride_head = out.stride(1);
+  a.num_parts = static_cast<int32_t>(parts.size(0));
+  a.num_seqs = static_cast<int32_t>(parts.size(1));
+  a.num_q_heads = static_cast<int32_t>(parts.size(2));
+  a.head_dim = static_cast<int32_t>(D);
+  a.dtype = out.scalar_type() == at::kBFloat16 ? DK_DTYPE_BFLOAT16 : DK_DTYPE_FLOAT16;
+  a.out_partial = as_partial ? 1 : 0;
+  const c10::cuda::OptionalCUDAGuard guard(parts.device());
+  const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(parts.device().index()).stream();
+  const int status = dk_merge_lse(&a, reinterpret_cast<dk_stream_t>(stream));
+  TORCH_CHECK(status == 0, "merge_lse failed: ", dk_last_error());
 }
 
 // Paged-KV write (dk_reshape_and_cache): key/value [T, Hkv, D] into caches
@@ -241,6 +302,10 @@ TORCH_LIBRARY(decode_kernels, m) {
       "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
       "Tensor! merge_counters) -> ()");
   m.def(
+      "paged_attention_decode_lse(Tensor! partial, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
+      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums) -> ()");
+  m.def("merge_lse(Tensor! out, Tensor parts) -> ()");
+  m.def(
       "reshape_and_cache(Tensor key, Tensor value, Tensor! key_cache, Tensor! value_cache, Tensor slot_mapping, "
       "float k_scale, float v_scale) -> ()");
 }
@@ -249,4 +314,6 @@ TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) {
   m.impl("paged_attention_decode", &paged_attention_decode);
   m.impl("paged_attention_decode_fused", &paged_attention_decode_fused);
   m.impl("reshape_and_cache", &reshape_and_cache);
+  m.impl("paged_attention_decode_lse", &paged_attention_decode_lse);
+  m.impl("merge_lse", &merge_lse);
 }

@@ -57,6 +57,14 @@ def _register_fakes() -> None:
     def _(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale):
         return None
 
+    @torch.library.register_fake("decode_kernels::paged_attention_decode_lse")
+    def _(partial, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums):
+        return None
+
+    @torch.library.register_fake("decode_kernels::merge_lse")
+    def _(out, parts):
+        return None
+
 
 try:
     if not TORCH_LIB_PATH.exists():
@@ -190,3 +198,54 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_cache: torch.T
     _require()
     torch.ops.decode_kernels.reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, float(k_scale),
                                                float(v_scale))
+
+
+def paged_attention_decode_lse(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    scale: float | None = None,
+    max_seq_len: int | None = None,
+    partial: torch.Tensor | None = None,
+    workspace: tuple | None = None,
+) -> torch.Tensor:
+    """Decode attention as fp32 partials: ``[num_seqs, num_q_heads, head_dim + 4]``
+    rows holding the normalised output ``o``, then ``lse = log(sum_t exp(scale * q.k_t))``
+    (``-inf`` and ``o = 0`` for an empty sequence), then 3 unused floats.
+
+    Partials of disjoint token ranges of the same sequences (the shards of a
+    sequence-sharded cache) combine exactly with :func:`merge_lse`.  Arguments
+    are as in :func:`paged_attention_decode`.
+    """
+    _require()
+    num_seqs, num_q_heads, head_dim = q.shape
+    if scale is None:
+        scale = head_dim**-0.5
+    if max_seq_len is None:
+        max_seq_len = int(seq_lens[:num_seqs].max().item()) if num_seqs > 0 else 0
+    if partial is None:
+        partial = torch.empty(num_seqs, num_q_heads, head_dim + 4, dtype=torch.float32, device=q.device)
+    if workspace is None:
+        kv_heads = k_cache.shape[2] if k_cache.dim() == 4 else None
+        bs = k_cache.shape[1] if k_cache.dim() == 4 else 16
+        workspace = alloc_workspace(num_seqs, num_q_heads, head_dim, max_seq_len, q.device, num_kv_heads=kv_heads,
+                                    block_size=bs)
+    tmp_out, max_logits, exp_sums = workspace[:3]
+    torch.ops.decode_kernels.paged_attention_decode_lse(partial, q, k_cache, v_cache, block_tables, seq_lens,
+                                                        float(scale), int(max_seq_len), tmp_out, max_logits,
+                                                        exp_sums)
+    return partial
+
+
+def merge_lse(parts: torch.Tensor, out: torch.Tensor | None = None, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Combine partials of disjoint token ranges, ``parts [R, n, Hq, D + 4]``
+    (from :func:`paged_attention_decode_lse`), into the attention output
+    ``[n, Hq, D]`` of ``out``'s dtype (``dtype`` when ``out`` is None), or into
+    merged fp32 partial rows when ``out`` is float32 ``[n, Hq, D + 4]``."""
+    _require()
+    if out is None:
+        out = torch.empty(parts.shape[1], parts.shape[2], parts.shape[3] - 4, dtype=dtype, device=parts.device)
+    torch.ops.decode_kernels.merge_lse(out, parts)
+    return out

@@ -1,4 +1,8 @@
-"""KV-head sharding of paged-attention decode across the GPUs of one node.
+"""Multi-GPU paged-attention decode on the GPUs of one node: KV-head
+sharding (``ShardedPagedAttention``) and sequence sharding
+(``SequenceShardedPagedAttention``).
+
+KV-head sharding.
 
 Attention is independent per KV head, and KV head ``h`` owns query heads
 ``[h*g, (h+1)*g)``.  Rank ``r`` of ``G`` therefore owns KV heads
@@ -9,6 +13,15 @@ data moves between ranks to compute a rank's heads, so a head-sharded
 consumer (a tensor-parallel o_proj) needs no collective at all; an NCCL
 all-gather of the per-head outputs is offered only for consumers that need
 every head on every rank (``gather=True``).
+
+Sequence sharding, for models whose KV heads cannot be split (MQA, or
+fewer KV heads than GPUs) and for long contexts at small batch: block ``j``
+of every sequence lives on rank ``j % G`` (block striping: balanced for any
+length, and a sequence that grows never moves a page).  Every rank holds the
+full query, computes fp32 partials ``(o, lse)`` over its own blocks
+(``paged_attention_decode_lse``), and one NCCL all-gather of the packed
+``[n, Hq, D + 4]`` rows lets every rank merge them with the log-sum-exp rule
+(``merge_lse``) -- exact, since the token sets are disjoint.
 
 The reference has no multi-GPU code; this layer is new.  Ranks are one
 process per GPU (``torch.distributed``, NCCL over NVLink/NVSwitch); the
@@ -127,3 +140,95 @@ class ShardedPagedAttention:
         if not gather or s.world == 1:
             return local
         return gather_heads(local, s, self.group)
+
+
+
+def stripe_tables(block_tables: torch.Tensor, seq_lens: torch.Tensor, block_size: int, rank: int, world: int):
+    """Rank ``rank``'s (block_tables, seq_lens) under block striping.
+
+    Block ``j`` of a sequence belongs to rank ``j % world``; the rank's table
+    row lists its blocks in order (contiguous int32 copy) and its length
+    counts their tokens (the sequence's last block may be partial).  Works on
+    CPU or device tensors; nothing leaves the device.  In a deployment each
+    rank keeps only its own rows and pages; this helper derives them from a
+    full table.
+    """
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    bt = block_tables[:, rank::world].contiguous()
+    L = seq_lens.to(torch.int64)
+    nb = (L + block_size - 1) // block_size
+    count = torch.clamp((nb - rank + world - 1) // world, min=0)
+    owns_last = (nb > 0) & ((nb - 1) % world == rank)
+    lens = count * block_size - torch.where(owns_last, nb * block_size - L, torch.zeros_like(L))
+    return bt, lens.to(torch.int32)
+
+
+def striped_max_len(max_seq_len: int, block_size: int, world: int) -> int:
+    """Upper bound of any rank's striped length (host-side, graph-safe)."""
+    blocks = -(-max_seq_len // block_size)
+    return -(-blocks // world) * block_size
+
+
+class SequenceShardedPagedAttention:
+    """Decode attention over block-striped sequence shards, merged on every rank.
+
+    ``lse_fn`` / ``merge_fn`` default to :func:`decodekernels_b200.paged_attention_decode_lse`
+    and :func:`decodekernels_b200.merge_lse` (the sm_100a kernels); tests of
+    the host-side logic on CPU ranks pass the CPU oracle instead.
+    """
+
+    def __init__(self, block_size: int, rank: int | None = None, world: int | None = None, group=None,
+                 lse_fn: Callable | None = None, merge_fn: Callable | None = None):
+        import torch.distributed as dist
+
+        if rank is None or world is None:
+            if dist.is_available() and dist.is_initialized():
+                rank, world = dist.get_rank(group), dist.get_world_size(group)
+            else:
+                rank, world = 0, 1
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside world {world}")
+        self.rank, self.world, self.group, self.block_size = rank, world, group, block_size
+        if lse_fn is None or merge_fn is None:
+            from .ops import merge_lse, paged_attention_decode_lse
+
+            lse_fn = lse_fn or paged_attention_decode_lse
+            merge_fn = merge_fn or merge_lse
+        self.lse_fn, self.merge_fn = lse_fn, merge_fn
+        self._gather_buf = None
+
+    def partial(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
+                max_seq_len=None, workspace=None) -> torch.Tensor:
+        """This rank's fp32 partial rows ``[n, Hq, D + 4]`` over its own blocks."""
+        if scale is None:
+            scale = q.shape[-1] ** -0.5
+        if max_seq_len is not None:
+            max_seq_len = striped_max_len(max_seq_len, self.block_size, self.world)
+        return self.lse_fn(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=scale,
+                           max_seq_len=max_seq_len, workspace=workspace)
+
+    def gather(self, partial: torch.Tensor) -> torch.Tensor:
+        """All-gather every rank's partial into ``[G, n, Hq, D + 4]`` (one
+        collective; the result lands in this rank's own memory)."""
+        import torch.distributed as dist
+
+        if self.world == 1:
+            return partial.unsqueeze(0)
+        shape = (self.world, *partial.shape)
+        if self._gather_buf is None or self._gather_buf.shape != shape or self._gather_buf.device != partial.device:
+            self._gather_buf = torch.empty(shape, dtype=partial.dtype, device=partial.device)
+        dist.all_gather_into_tensor(self._gather_buf.view(-1), partial.contiguous().view(-1), group=self.group)
+        return self._gather_buf
+
+    def __call__(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
+                 max_seq_len=None, out=None, workspace=None) -> torch.Tensor:
+        """Full attention output ``[n, Hq, D]`` (q's dtype) on every rank.
+
+        ``max_seq_len`` is the longest WHOLE sequence (the local bound is
+        derived from it); ``seq_lens_local`` / ``block_tables_local`` are this
+        rank's striped lengths and blocks (:func:`stripe_tables`).
+        """
+        parts = self.gather(self.partial(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale,
+                                         max_seq_len, workspace))
+        return self.merge_fn(parts, out=out, dtype=q.dtype)

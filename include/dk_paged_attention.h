@@ -175,6 +175,38 @@ DK_API int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t
                           int32_t max_seq_len, int32_t device);
 
 /*
+ * Decode into fp32 partials instead of `out`: the building block of
+ * sequence-sharded decode, where each GPU holds a token range of every
+ * sequence (no counterpart in DecodeKernels, which runs on one GPU).
+ * partial: float [num_seqs, num_q_heads, head_dim + 4], 16-byte aligned; row
+ * (seq, q_head) holds the normalised output o (head_dim floats), then
+ * lse = log(sum_t exp(scale * q.k_t)) over the sequence's tokens (natural
+ * log; -inf and o = 0 for an empty sequence), then 3 unused floats.
+ * args->out and its strides are ignored; everything else is as in
+ * dk_paged_attention_decode (same planner, workspace and merge counters).
+ */
+DK_API int dk_paged_attention_decode_lse(const DkPagedAttnArgs* args, float* partial, dk_stream_t stream);
+
+/*
+ * Merge partials of disjoint token ranges (dk_paged_attention_decode_lse on
+ * each shard):  M = max_r lse_r,  w_r = exp(lse_r - M),
+ *   out = sum_r w_r o_r / sum_r w_r,  lse = M + log(sum_r w_r)
+ * (zeros and lse = -inf when every part is empty).
+ */
+typedef struct DkLseMergeArgs {
+  const float* parts;      /* num_parts partial buffers [num_seqs, num_q_heads, head_dim + 4] */
+  int64_t part_stride;     /* floats from one part to the next (>= num_seqs * num_q_heads * (head_dim + 4)) */
+  void* out;               /* [num_seqs, num_q_heads, head_dim] of `dtype`, or partial rows when out_partial */
+  int64_t out_stride_seq;  /* elements (floats when out_partial) */
+  int64_t out_stride_head;
+  int32_t num_parts, num_seqs, num_q_heads, head_dim;
+  int32_t dtype;           /* DK_DTYPE_FLOAT16 / DK_DTYPE_BFLOAT16 of out (ignored when out_partial) */
+  int32_t out_partial;     /* 1: write merged (o, lse, pad) fp32 rows, for merging in stages */
+} DkLseMergeArgs;
+
+DK_API int dk_merge_lse(const DkLseMergeArgs* args, dk_stream_t stream);
+
+/*
  * Paged-KV write, the step before decode: no counterpart in DecodeKernels
  * (its decode reads caches that vLLM's reshape_and_cache_flash wrote); this
  * is that operation.  For every token t with slot = slot_mapping[t] in
