@@ -259,22 +259,45 @@ def run_gpu_arm(args) -> None:
     if not dk.is_available():
         raise SystemExit(f"decodekernels_b200 native library unavailable: {dk.ops._IMPORT_ERROR}")
 
-    batch = workloads.make(args.workload, dev, shard=(rank, world))
+    cfg = workloads.CONFIGS[args.workload]
+    sharding = args.sharding
+    if sharding == "auto":
+        sharding = "head" if cfg.num_kv_heads % world == 0 else "seq"
+    seq_mode = world > 1 and sharding == "seq"
+    if seq_mode:
+        # Sequence sharding: every rank holds its striped blocks of every
+        # sequence and the whole query; a step is the rank's partials, one
+        # NCCL all-gather of them and the log-sum-exp merge (full output on
+        # every rank).
+        from decodekernels_b200.sharded import SequenceShardedPagedAttention, striped_max_len
+
+        batch = workloads.make_striped(args.workload, dev, stripe=(rank, world))
+        seq_attn = SequenceShardedPagedAttention(block_size=batch.config.block_size, rank=rank, world=world)
+        full_max = max(workloads.seq_lens(args.workload))
+        max_len = striped_max_len(full_max, batch.config.block_size, world)
+    else:
+        batch = workloads.make(args.workload, dev, shard=(rank, world))
+        max_len = batch.max_seq_len
     q, kv = batch.q, batch.kv
     n, hq, d = q.shape
-    max_len = batch.max_seq_len
     out = torch.empty_like(q)
     ws = dk.alloc_workspace(n, hq, d, max_len, dev, num_kv_heads=kv.k_cache.shape[2],
-                            block_size=kv.block_size, merge_counters=True)
+                            block_size=kv.block_size, merge_counters=not seq_mode)
     plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, ws)
 
-    def step():
-        dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=max_len,
-                                  out=out, workspace=ws)
+    if seq_mode:
+        def step():
+            seq_attn(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=full_max, out=out,
+                     workspace=ws)
+    else:
+        def step():
+            dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=max_len,
+                                      out=out, workspace=ws)
 
     step()
     torch.cuda.synchronize()
-    parity = _check_parity(batch, out, rank)
+    parity = _check_parity(batch, out, rank) if not seq_mode else {
+        "checked": "sequence-sharded merge parity is covered by tests/test_gpu_seq_sharded.py"}
 
     # Inputs several times the 126 MB L2 (c2-c5) stream through it with no
     # reuse between steps; smaller ones (c1) get a 256 MB write between steps.
@@ -315,7 +338,7 @@ def run_gpu_arm(args) -> None:
     # With N GPUs, also time the variant whose consumer needs every head on
     # every rank: decode + NCCL all-gather of the per-head outputs.
     gather_s = None
-    if world > 1:
+    if world > 1 and not seq_mode:
         from decodekernels_b200.sharded import gather_heads, head_shard
 
         shard = head_shard(batch.config.num_q_heads, batch.config.num_kv_heads, rank, world)
@@ -346,8 +369,11 @@ def run_gpu_arm(args) -> None:
         q_dev.copy_(h_q, non_blocking=True)
         bt_dev.copy_(h_bt, non_blocking=True)
         sl_dev.copy_(h_sl, non_blocking=True)
-        dk.paged_attention_decode(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=max_len, out=out,
-                                  workspace=ws)
+        if seq_mode:
+            seq_attn(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=full_max, out=out, workspace=ws)
+        else:
+            dk.paged_attention_decode(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=max_len, out=out,
+                                      workspace=ws)
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(max(args.warmup, 3)):
@@ -409,7 +435,9 @@ def run_gpu_arm(args) -> None:
                 "num_seqs": n, "num_q_heads": batch.config.num_q_heads, "num_kv_heads": batch.config.num_kv_heads,
                 "head_dim": d, "block_size": kv.block_size, "max_seq_len": max_len,
                 "kv_bytes_total": kv_total, "algorithmic_bytes_total": alg_total,
-                "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                "parallelism": (f"sequence shard (block-striped) x{world}, NCCL all-gather of partials + "
+                                "LSE merge in every step" if seq_mode else f"kv-head shard x{world}")
+                               if world > 1 else "single GPU",
                 "l2": "L2 flushed (256 MB write) before every step" if flush else
                       "inputs larger than L2 (no flush between steps)",
                 "plan": plan, "parity": parity,
@@ -423,7 +451,7 @@ def run_gpu_arm(args) -> None:
             },
             "e2e": {"value": kv_total / (e2e_s / e_steps) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e_steps, "api": "decodekernels_b200.paged_attention_decode"},
-            "gpu_launches": args.steps * plan["launches"],
+            "gpu_launches": args.steps * (plan["launches"] + (1 if seq_mode else 0)),
             "with_gather": None if not gather_s else {
                 "us_per_call": gather_s / args.steps * 1e6, "value": kv_total / (gather_s / args.steps) / 1e12,
                 "unit": UNIT, "note": "decode + NCCL all-gather of the per-head outputs to every rank"},
@@ -448,6 +476,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--sharding", default="auto", choices=["auto", "head", "seq"],
+                    help="N>1: KV-head sharding (no exchange) or block-striped sequence sharding (partials "
+                         "all-gathered and merged every step); auto = head when the KV heads divide evenly")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -111,9 +111,52 @@ def _layout_views(buf: torch.Tensor, layout: str, head_dim: int):
     raise ValueError(layout)
 
 
+def make_striped(name: str, device="cuda", stripe: tuple[int, int] = (0, 1), seed: int = 0) -> Batch:
+    """Rank ``rank``'s part of config ``name`` under sequence (block-striped)
+    sharding over ``world`` GPUs: block ``j`` of every sequence lives on rank
+    ``j % world``.  The rank holds the whole query batch (all heads, the same
+    draw on every rank), only its own blocks (a compact pool with its own
+    block tables) and its striped lengths.  ``Batch.lens`` are those local
+    lengths, so ``kv_bytes`` is what this rank reads."""
+    c = CONFIGS[name]
+    rank, world = stripe
+    bs, d, hkv = c.block_size, c.head_dim, c.num_kv_heads
+    full = seq_lens(name)
+    nblk = [-(-L // bs) for L in full]
+    mine = [len(range(rank, nb, world)) for nb in nblk]
+    lens = []
+    for L, nb, cnt in zip(full, nblk, mine):
+        last_mine = nb > 0 and (nb - 1) % world == rank
+        lens.append(cnt * bs - (nb * bs - L if last_mine else 0))
+    need = sum(mine)
+    pool = need + 16
+    gen = torch.Generator(device=device).manual_seed(seed * 1000 + 100 + rank)
+    if c.layout == "vllm":
+        buf = torch.randn(pool, hkv, bs, 2 * d, generator=gen, device=device, dtype=c.dtype)
+    elif c.layout == "hnd":
+        buf = torch.randn(2, pool, hkv, bs, d, generator=gen, device=device, dtype=c.dtype)
+    else:
+        buf = torch.randn(2, pool, bs, hkv, d, generator=gen, device=device, dtype=c.dtype)
+    if c.sigma != 1.0:
+        buf.mul_(c.sigma)
+    k, v = _layout_views(buf, c.layout, d)
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(seed + 7 + rank)).to(torch.int32)
+    width = max(max(mine) if mine else 1, 1)
+    tables = torch.zeros(len(full), width, dtype=torch.int32)
+    off = 0
+    for i, cnt in enumerate(mine):
+        tables[i, :cnt] = perm[off : off + cnt]
+        off += cnt
+    qg = torch.Generator(device=device).manual_seed(seed * 1000 + 500)  # same query on every rank
+    q = torch.randn(len(full), c.num_q_heads, d, generator=qg, device=device, dtype=c.dtype)
+    kv = PagedKV(k, v, tables.to(device), torch.tensor(lens, dtype=torch.int32, device=device), bs)
+    return Batch(c, q, kv, lens, rank, world, hkv)
+
+
 def make(name: str, device="cuda", shard: tuple[int, int] = (0, 1), seed: int = 0,
          seqs: list[int] | None = None) -> Batch:
-    """Build config ``name`` (or only sequences ``seqs`` of it) on ``device``."""
+    """Build config ``name`` (or only sequences ``seqs`` of it) on ``device``;
+    ``shard = (rank, world)`` keeps rank ``rank``'s KV heads (head sharding)."""
     c = CONFIGS[name]
     rank, world = shard
     if c.num_kv_heads % world:

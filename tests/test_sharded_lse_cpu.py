@@ -127,3 +127,25 @@ def test_two_gloo_ranks_match_the_whole_batch():
 def test_dead_rank_fails_the_exchange_instead_of_hanging():
     outdir = _run("dead")
     assert os.path.exists(os.path.join(outdir, "rank0.err")), "rank 0 finished an exchange whose peer had exited"
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_striped_workload_builder(world):
+    """bench.py's sequence-sharded batches: the ranks' lengths add up to the
+    config's, every rank holds the same queries, and each table only names
+    blocks of the rank's own pool."""
+    from decodekernels_b200 import workloads
+
+    full = workloads.seq_lens("c1")
+    total = np.zeros(len(full), dtype=np.int64)
+    q0 = None
+    for r in range(world):
+        b = workloads.make_striped("c1", "cpu", stripe=(r, world))
+        total += np.array(b.lens)
+        assert b.kv.seq_lens.tolist() == b.lens
+        assert int(b.kv.block_tables.max()) < b.kv.k_cache.shape[0]
+        q0 = b.q if q0 is None else q0
+        assert torch.equal(b.q, q0)
+        want_bt, want_lens = sl.stripe(np.zeros((len(full), 64), np.int32), full, 16, r, world)
+        assert b.lens == want_lens.tolist()
+    assert total.tolist() == full
