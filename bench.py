@@ -144,7 +144,7 @@ def _cpu_sample(workload: str, target_bytes: float):
 
     lens = workloads.seq_lens(workload)
     c = workloads.CONFIGS[workload]
-    per_tok = c.num_kv_heads * c.head_dim * 2 * (torch.finfo(c.dtype).bits // 8)
+    per_tok = c.num_kv_heads * c.head_dim * 2 * c.kv_bytes_per_elem
     order = torch.randperm(len(lens), generator=torch.Generator().manual_seed(11)).tolist()
     chosen, total = [], 0
     for i in order:
@@ -156,6 +156,14 @@ def _cpu_sample(workload: str, target_bytes: float):
             break
     batch = workloads.make(workload, "cpu", seqs=sorted(chosen))
     return batch
+
+
+def workloads_dequantize(batch):
+    """A CPU sample's cache as 16-bit values (e4m3 configs: code * scale,
+    exact), for the 16-bit C oracle."""
+    from decodekernels_b200 import workloads
+
+    return workloads.dequantize(batch.kv, batch.config)
 
 
 def workloads_lens(workload: str) -> list[int]:
@@ -170,7 +178,8 @@ def cpu_throughput(workload: str, seconds: float, target_bytes: float = 256e6, s
     from oracle import native
 
     b = _cpu_sample(workload, target_bytes)
-    args = (b.q, b.kv.k_cache, b.kv.v_cache, b.kv.block_tables, b.kv.seq_lens)
+    kv = workloads_dequantize(b)
+    args = (b.q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens)
     for _ in range(warmup):
         native.dense_c(*args)
     times = []
@@ -188,7 +197,8 @@ def cpu_throughput(workload: str, seconds: float, target_bytes: float = 256e6, s
         "kind": "port",
         "sample": f"{len(b.lens)} of {len(workloads_lens(workload))} sequences of {workload} "
                   f"({sum(b.lens)} tokens, {kvb / 1e6:.0f} MB KV), median of {len(times)} calls of the oracle's "
-                  f"C port (OpenMP, all host threads)",
+                  f"C port (OpenMP, all host threads)" + (" on the caches dequantised to 16 bits (the reference "
+                                                          "has no e4m3 path)" if b.config.kv_fp8 else ""),
         "seconds_per_call": per_call,
         "calls": len(times),
     }
@@ -230,6 +240,7 @@ def _check_parity(batch, out, rank) -> dict:
     pick = sorted(set([live[0], max(live, key=lambda i: lens[i]), min(live, key=lambda i: lens[i])]
                       + [i for i, L in enumerate(lens) if L == 0][:1]))
     q, kv = workloads.compact_sequences(batch, pick)
+    kv = workloads.dequantize(kv, batch.config)  # e4m3 configs: the exact 16-bit values of the codes
     ref = native.dense_c(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens)
     got = out[pick].float().cpu().numpy()
     err = np.abs(got - ref)
@@ -283,16 +294,20 @@ def run_gpu_arm(args) -> None:
     out = torch.empty_like(q)
     ws = dk.alloc_workspace(n, hq, d, max_len, dev, num_kv_heads=kv.k_cache.shape[2],
                             block_size=kv.block_size, merge_counters=not seq_mode)
-    plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, ws)
+    fp8_scale = batch.config.kv_scale if batch.config.kv_fp8 else 1.0
+    plan = capi.plan(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, ws,
+                     k_scale=fp8_scale, v_scale=fp8_scale)
 
     if seq_mode:
         def step():
             seq_attn(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=full_max, out=out,
-                     workspace=ws)
+                     workspace=ws, k_scale=fp8_scale, v_scale=fp8_scale)
     else:
+        kscale = batch.config.kv_scale if batch.config.kv_fp8 else 1.0
+
         def step():
             dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=max_len,
-                                      out=out, workspace=ws)
+                                      out=out, workspace=ws, k_scale=kscale, v_scale=kscale)
 
     step()
     torch.cuda.synchronize()
@@ -370,10 +385,11 @@ def run_gpu_arm(args) -> None:
         bt_dev.copy_(h_bt, non_blocking=True)
         sl_dev.copy_(h_sl, non_blocking=True)
         if seq_mode:
-            seq_attn(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=full_max, out=out, workspace=ws)
+            seq_attn(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=full_max, out=out, workspace=ws,
+                     k_scale=fp8_scale, v_scale=fp8_scale)
         else:
             dk.paged_attention_decode(q_dev, kv.k_cache, kv.v_cache, bt_dev, sl_dev, max_seq_len=max_len, out=out,
-                                      workspace=ws)
+                                      workspace=ws, k_scale=kscale, v_scale=kscale)
         h_out.copy_(out, non_blocking=True)
 
     for _ in range(max(args.warmup, 3)):
@@ -427,8 +443,10 @@ def run_gpu_arm(args) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_s * 1e3, "us_per_call": step_s * 1e6,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16" if
-            batch.config.dtype == torch.float16 else "bf16", "accumulate": "f32", "data": "synthetic",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": ("e4m3 KV, f16 mma" if batch.config.kv_fp8 else
+                      ("f16" if batch.config.dtype == torch.float16 else "bf16")),
+            "accumulate": "f32", "data": "synthetic",
             "impl": "ours",
             "config": {
                 "workload": f"{args.workload}: {batch.config.description}",
@@ -475,7 +493,8 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c5",
+                    choices=["c1", "c2", "c3", "c4", "c5", "c2f8", "c3f8", "c4f8", "c5f8"])
     ap.add_argument("--sharding", default="auto", choices=["auto", "head", "seq"],
                     help="N>1: KV-head sharding (no exchange) or block-striped sequence sharding (partials "
                          "all-gathered and merged every step); auto = head when the KV heads divide evenly")

@@ -70,6 +70,9 @@ class DkPagedAttnArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("scale", ctypes.c_float),
+        ("kv_fp8", ctypes.c_int32),
+        ("k_scale", ctypes.c_float),
+        ("v_scale", ctypes.c_float),
     ]
 
 
@@ -128,6 +131,7 @@ class DkPlan(ctypes.Structure):
         ("stages", ctypes.c_int32),
         ("smem_bytes", ctypes.c_int32),
         ("launches", ctypes.c_int32),
+        ("ctas_per_sm", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict:
@@ -207,8 +211,10 @@ def _dtype_code(t) -> int:
 
 
 def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-              partition_size: int = 0, force_simt: bool = False, flags: int = 0) -> DkPagedAttnArgs:
-    """Fill the C struct from tensors (pointers + element strides)."""
+              partition_size: int = 0, force_simt: bool = False, flags: int = 0, k_scale: float = 1.0,
+              v_scale: float = 1.0) -> DkPagedAttnArgs:
+    """Fill the C struct from tensors (pointers + element strides).  A uint8 /
+    float8_e4m3fn cache is read as e4m3 with the per-tensor scales."""
     a = DkPagedAttnArgs()
     a.out = out.data_ptr()
     a.q = q.data_ptr()
@@ -236,13 +242,16 @@ def make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, o
     a.dtype = _dtype_code(q)
     a.flags = (DK_FLAG_FORCE_SIMT if force_simt else 0) | flags
     a.scale = float(scale)
+    a.kv_fp8 = 1 if _cache_dtype_code(k_cache) == DK_DTYPE_FP8_E4M3 else 0
+    a.k_scale, a.v_scale = float(k_scale), float(v_scale)
     return a
 
 
 def plan(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-         partition_size: int = 0, force_simt: bool = False, flags: int = 0) -> dict:
+         partition_size: int = 0, force_simt: bool = False, flags: int = 0, k_scale: float = 1.0,
+         v_scale: float = 1.0) -> dict:
     a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
-                  force_simt, flags)
+                  force_simt, flags, k_scale, v_scale)
     p = DkPlan()
     rc = load().dk_plan(ctypes.byref(a), ctypes.byref(p))
     if rc != 0:
@@ -251,14 +260,15 @@ def plan(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, w
 
 
 def decode(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace=None,
-           partition_size: int = 0, force_simt: bool = False, stream=None, flags: int = 0) -> int:
+           partition_size: int = 0, force_simt: bool = False, stream=None, flags: int = 0, k_scale: float = 1.0,
+           v_scale: float = 1.0) -> int:
     """dk_paged_attention_decode on ``stream`` (default: torch's current stream).
 
     Returns 0; raises RuntimeError with the library's message otherwise."""
     import torch
 
     a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, partition_size,
-                  force_simt, flags)
+                  force_simt, flags, k_scale, v_scale)
     if stream is None:
         stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
     rc = load().dk_paged_attention_decode(ctypes.byref(a), ctypes.c_void_p(stream))
@@ -328,12 +338,13 @@ def reshape_and_cache(key, value, key_cache, value_cache, slot_mapping, k_scale:
 
 
 def decode_lse(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, partial, workspace=None,
-               partition_size: int = 0, stream=None, flags: int = 0) -> int:
+               partition_size: int = 0, stream=None, flags: int = 0, k_scale: float = 1.0,
+               v_scale: float = 1.0) -> int:
     """dk_paged_attention_decode_lse: fp32 rows (o, lse, pad) into ``partial`` [n, Hq, D + 4]."""
     import torch
 
     a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, partial, workspace, partition_size,
-                  False, flags)
+                  False, flags, k_scale, v_scale)
     if stream is None:
         stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
     rc = load().dk_paged_attention_decode_lse(ctypes.byref(a), ctypes.c_void_p(partial.data_ptr()),

@@ -46,7 +46,9 @@ struct DecodeParams {
   int split;           // 1: partitions write the workspace and the merge kernel writes out
   int kv_fused;        // 1: one tensor map covers K and V (vLLM's interleaved K|V rows)
   int lse_mode;        // 1: `out` is fp32 rows [o (head_dim) | lse | 3 pad] per (seq, q_head), not T
-  float scale_log2;    // softmax scale * log2(e)
+  float scale_log2;    // softmax scale * log2(e) (* k_scale for e4m3 caches)
+  float v_scale;       // e4m3 caches: V = code * v_scale (1 otherwise), applied to the partition results
+  int kv_fp8;          // 1: the caches hold e4m3 bytes
 };
 
 }  // namespace dkb

@@ -193,6 +193,27 @@ struct Conv<__half> {
 };
 
 // Two raw 16-bit elements packed low-first, without any conversion.
+// Two e4m3 values (low byte = element 0) -> f16x2 (low half = element 0);
+// exact: every e4m3 value is an f16 value.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t y;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(y) : "r"(two_bytes));
+  return y;
+}
+
+// Byte permute: result byte i = byte (sel >> 4i) & 7 of {b:a} (a = bytes 0-3).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t y;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(y) : "r"(a), "r"(b), "r"(sel));
+  return y;
+}
+
+// One e4m3 byte -> float (exact).
+__device__ __forceinline__ float e4m3_to_f32(uint8_t x) {
+  const uint32_t h2 = e4m3x2_to_f16x2(x);
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+
 __device__ __forceinline__ uint32_t pack_raw16(uint16_t lo, uint16_t hi) {
   return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }

@@ -28,8 +28,9 @@
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 400;  // 0.4.0: dk_paged_attention_decode_lse / dk_merge_lse (0.3.0: dk_reshape_and_cache;
-                                // 0.2.0: DkPagedAttnArgs.merge_counters)
+constexpr int kVersion = 500;  // 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
+                                // dk_paged_attention_decode_lse / dk_merge_lse; 0.3.0: dk_reshape_and_cache;
+                                // 0.2.0: DkPagedAttnArgs.merge_counters
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
 // at least kMinPartition tokens (overridable for tuning sweeps).
@@ -94,11 +95,25 @@ constexpr int tma_stages() {
   return TmaShape<D>::kStages;
 }
 
+// e4m3 caches: half the bytes per tile, so a deeper ring keeps as many bytes
+// in flight per CTA.
+#ifndef DK_TMA_FP8_STAGES
+#define DK_TMA_FP8_STAGES 4
+#endif
+template <int D>
+struct TmaShapeFp8 {
+  static constexpr int kStages = DK_TMA_FP8_STAGES;
+  static constexpr int kWarps = TmaShape<D>::kWarps;
+  using Cfg = TmaConfig<D, kStages, kWarps, 1>;
+};
+
 int tma_tile(int D) {
   return D == 64 ? TmaShape<64>::Cfg::kTile : (D == 128 ? TmaShape<128>::Cfg::kTile : TmaShape<256>::Cfg::kTile);
 }
 
-int smem_for(int path, int D) {
+int smem_for(int path, int D, bool fp8 = false) {
+  if (path == DK_PATH_TMA_MMA && fp8) return D == 128 ? TmaShapeFp8<128>::Cfg::kSmemBytes
+                                                      : TmaShapeFp8<256>::Cfg::kSmemBytes;
   if (path == DK_PATH_TMA_MMA) {
     switch (D) {
       case 64: return TmaShape<64>::Cfg::kSmemBytes;
@@ -137,11 +152,16 @@ int num_sms(int dev) {
 // Opt every kernel that needs more than 48 KB of dynamic shared memory in,
 // once per (kernel, device).
 template <typename Kernel>
+// Dynamic shared memory above 48 KB needs an opt-in, and the partition
+// kernels want the whole carveout as shared memory (their KV traffic bypasses
+// L1) so that as many CTAs as the ring allows stay resident.
 cudaError_t ensure_smem_attr(Kernel kernel, int smem, int dev, bool* done) {
-  if (smem <= 48 * 1024) return cudaSuccess;
   std::lock_guard<std::mutex> lk(g_dev_mu);
   if (dev >= 0 && dev < kMaxDevices && done[dev]) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaSuccess;
+  if (smem > 48 * 1024) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) done[dev] = true;
   return e;
 }
@@ -167,6 +187,9 @@ int validate(const DkPagedAttnArgs* a) {
   if (a->max_partitions < 0) return fail(1, "max_partitions must be non-negative");
   if (a->partition_size < 0 || a->partition_size % DK_TILE_TOKENS != 0)
     return fail(1, "partition_size must be 0 (planner) or a positive multiple of %d", DK_TILE_TOKENS);
+  if (a->kv_fp8 != 0 && a->kv_fp8 != 1) return fail(1, "kv_fp8 must be 0 or 1");
+  if (a->kv_fp8 && !(a->k_scale > 0.0f && a->v_scale > 0.0f && a->k_scale < INFINITY && a->v_scale < INFINITY))
+    return fail(1, "fp8 KV cache: k_scale and v_scale must be positive and finite");
   if (a->num_seqs == 0) return 0;
   if (!a->out || !a->q || !a->k_cache || !a->v_cache || !a->block_tables || !a->seq_lens)
     return fail(1, "paged_attention_decode: NULL tensor pointer");
@@ -178,8 +201,9 @@ int validate(const DkPagedAttnArgs* a) {
   for (int64_t s : strides) {
     if (s < 0 || s % vec != 0) return fail(1, "KV-cache strides must be multiples of head_dim / 32 for vectorised loads");
   }
-  if (!aligned(a->k_cache, static_cast<size_t>(vec * 2)) || !aligned(a->v_cache, static_cast<size_t>(vec * 2)))
-    return fail(1, "KV-cache pointers must be aligned to head_dim / 16 bytes");
+  const size_t esz = a->kv_fp8 ? 1 : 2;
+  if (!aligned(a->k_cache, static_cast<size_t>(vec) * esz) || !aligned(a->v_cache, static_cast<size_t>(vec) * esz))
+    return fail(1, "KV-cache pointers must be aligned to head_dim / 32 elements");
   if (a->max_partitions > 0 && (!a->tmp_out || !a->max_logits || !a->exp_sums))
     return fail(1, "split-K workspace pointers are NULL but max_partitions > 0");
   if (a->max_partitions > 0 && (!aligned(a->tmp_out, 16) || !aligned(a->max_logits, 4) || !aligned(a->exp_sums, 4)))
@@ -216,11 +240,11 @@ constexpr long long kFusedMergeMaxBytes = DK_FUSED_MERGE_MAX_BYTES;
 constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
 constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
 
-int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms) {
+int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms, int kv_bytes = 2) {
   const long long pairs = std::max<long long>(1, static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1));
   const long long slots = static_cast<long long>(kPlanCtasPerSm) * sms;
   const long long work = pairs * std::max(max_seq_len, 1);
-  const long long token_bytes = 4LL * head_dim;  // K + V, 16-bit elements
+  const long long token_bytes = 2LL * kv_bytes * head_dim;  // K + V
   int ps = round_up((work + slots - 1) / slots, DK_TILE_TOKENS);
   long long cap = kMaxBytes / token_bytes;
   if (num_seqs > 1 && pairs < 4 * slots) cap = std::min(cap, kVariedBytes / token_bytes);
@@ -236,14 +260,16 @@ bool tma_eligible(const DkPagedAttnArgs& a) {
   if (a.flags & DK_FLAG_FORCE_SIMT) return false;
   const int bs = a.block_size;
   if (bs < 8 || (bs & (bs - 1)) != 0) return false;
+  if (a.kv_fp8 && a.head_dim < 128) return false;  // e4m3 rows shorter than a 128-byte swizzle row
+  const int64_t esz = a.kv_fp8 ? 1 : 2;
   if (!aligned(a.k_cache, 16) || !aligned(a.v_cache, 16)) return false;
   const int64_t sizes[3] = {a.num_blocks, a.block_size, a.num_kv_heads};
   const int64_t ks[3] = {a.k_stride_block, a.k_stride_token, a.k_stride_head};
   const int64_t vs[3] = {a.v_stride_block, a.v_stride_token, a.v_stride_head};
   for (int i = 0; i < 3; ++i) {
     if (sizes[i] <= 1) continue;  // the coordinate is always 0; the stride is never used
-    if ((ks[i] * 2) % 16 != 0 || (vs[i] * 2) % 16 != 0) return false;
-    if (ks[i] * 2 >= (int64_t(1) << 40) || vs[i] * 2 >= (int64_t(1) << 40)) return false;
+    if ((ks[i] * esz) % 16 != 0 || (vs[i] * esz) % 16 != 0) return false;
+    if (ks[i] * esz >= (int64_t(1) << 40) || vs[i] * esz >= (int64_t(1) << 40)) return false;
   }
   return true;
 }
@@ -251,7 +277,7 @@ bool tma_eligible(const DkPagedAttnArgs& a) {
 // K and V are the two halves of one row (vLLM's [blocks, heads, bs, 2*D]
 // buffer viewed as two [blocks, bs, heads, D] tensors): one map covers both.
 bool kv_fused(const DkPagedAttnArgs& a) {
-  return static_cast<const char*>(a.v_cache) == static_cast<const char*>(a.k_cache) + a.head_dim * 2 &&
+  return static_cast<const char*>(a.v_cache) == static_cast<const char*>(a.k_cache) + a.head_dim * (a.kv_fp8 ? 1 : 2) &&
          a.k_stride_block == a.v_stride_block && a.k_stride_token == a.v_stride_token &&
          a.k_stride_head == a.v_stride_head;
 }
@@ -279,7 +305,8 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
     parts = 1;
   } else {
     ps = a.partition_size > 0 ? a.partition_size
-                              : desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L, num_sms(dev));
+                              : desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L, num_sms(dev),
+                                                       a.kv_fp8 ? 1 : 2);
     parts = ceil_div(L, ps);
     if (parts > a.max_partitions) {  // the caller's workspace caps the partition count
       ps = round_up(ceil_div(L, a.max_partitions), DK_TILE_TOKENS);
@@ -290,10 +317,11 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   pl->num_partitions = parts;
   pl->split = parts > 1 ? 1 : 0;
   pl->num_ctas = static_cast<int32_t>(std::min<long long>(INT_MAX, 1LL * parts * a.num_kv_heads * a.num_seqs));
-  pl->stages = pl->path == DK_PATH_TMA_MMA
-                   ? (a.head_dim == 64 ? tma_stages<64>() : (a.head_dim == 128 ? tma_stages<128>() : tma_stages<256>()))
-                   : 0;
-  pl->smem_bytes = smem_for(pl->path, a.head_dim);
+  pl->stages = pl->path != DK_PATH_TMA_MMA ? 0
+               : a.kv_fp8                 ? DK_TMA_FP8_STAGES
+                                          : (a.head_dim == 64 ? tma_stages<64>()
+                                                              : (a.head_dim == 128 ? tma_stages<128>() : tma_stages<256>()));
+  pl->smem_bytes = smem_for(pl->path, a.head_dim, a.kv_fp8 != 0);
   // Merge counters turn the merge into the last partition's epilogue, which
   // saves the merge kernel's launch and latency but costs every partition a
   // release + atomic round trip and leaves each pair's merge to one CTA.
@@ -332,6 +360,7 @@ EncodeTiledFn encode_fn() {
 
 struct MapKey {
   const void* ptr;
+  int esz;
   int64_t strides[3];
   int64_t sizes[3];
   int rows;
@@ -356,11 +385,14 @@ int g_map_next = 0;
 // (2 B, token stride, 128 B, head stride, block stride).  The box is all
 // `col_blocks` column blocks of `rows` token rows of one head of one page and
 // lands in shared memory as [column block][row][128 B], 128-byte swizzled.
+// esz: element size (2, or 1 for e4m3 bytes); a 128-byte column block holds
+// 128 / esz elements.
 int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, int64_t num_blocks, int block_size,
-              int num_kv_heads, int col_blocks, int rows, int dev, CUtensorMap* out) {
+              int num_kv_heads, int col_blocks, int rows, int dev, CUtensorMap* out, int esz = 2) {
   MapKey key;
   std::memset(&key, 0, sizeof(key));
   key.ptr = ptr;
+  key.esz = esz;
   key.strides[0] = s_head;
   key.strides[1] = s_tok;
   key.strides[2] = s_block;
@@ -382,18 +414,20 @@ int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, i
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(static_cast<int>(cudaErrorNotSupported), "cuTensorMapEncodeTiled is unavailable");
   // a dimension of size 1 is never stepped: any legal stride will do
-  auto legal = [](int64_t size, int64_t stride_elems) -> cuuint64_t {
-    const int64_t b = stride_elems * 2;
+  auto legal = [esz](int64_t size, int64_t stride_elems) -> cuuint64_t {
+    const int64_t b = stride_elems * esz;
     return static_cast<cuuint64_t>(size <= 1 || b <= 0 || b % 16 != 0 ? 16 : b);
   };
-  const cuuint64_t gdim[5] = {64, static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(col_blocks),
+  const cuuint32_t inner = static_cast<cuuint32_t>(128 / esz);
+  const cuuint64_t gdim[5] = {inner, static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(col_blocks),
                               static_cast<cuuint64_t>(num_kv_heads), static_cast<cuuint64_t>(num_blocks)};
   const cuuint64_t gstride[4] = {legal(block_size, s_tok), 128, legal(num_kv_heads, s_head),
                                  legal(num_blocks, s_block)};
-  const cuuint32_t box[5] = {64, static_cast<cuuint32_t>(rows), static_cast<cuuint32_t>(col_blocks), 1, 1};
+  const cuuint32_t box[5] = {inner, static_cast<cuuint32_t>(rows), static_cast<cuuint32_t>(col_blocks), 1, 1};
   const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
-  CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 5, const_cast<void*>(ptr), gdim, gstride, box, estride,
+  CUresult r = fn(&map, esz == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 5,
+                  const_cast<void*>(ptr), gdim, gstride, box, estride,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(1, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
@@ -430,15 +464,72 @@ template <int D>
 int build_maps(const DkPagedAttnArgs& a, DecodeParams& p, int dev, CUtensorMap* kmap, CUtensorMap* vmap) {
   const int rows = 1 << p.rows_log2;
   p.kv_fused = kv_fused(a) ? 1 : 0;
+  const int esz = a.kv_fp8 ? 1 : 2;
+  const int cols = D * esz / 128;  // 128-byte column blocks of one K (or V) row
   if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
-                        a.num_kv_heads, (p.kv_fused ? 2 : 1) * (D / 64), rows, dev, kmap))
+                        a.num_kv_heads, (p.kv_fused ? 2 : 1) * cols, rows, dev, kmap, esz))
     return r;
   if (p.kv_fused) {
     *vmap = *kmap;  // unused
     return 0;
   }
   return build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks, a.block_size,
-                   a.num_kv_heads, D / 64, rows, dev, vmap);
+                   a.num_kv_heads, cols, rows, dev, vmap, esz);
+}
+
+// Resident CTAs per SM of the partition kernel a plan launches (0 when it
+// cannot be queried, e.g. without a GPU).
+template <typename Kernel>
+int occupancy_of(Kernel kernel, int threads, int smem, int dev, bool* attr_done) {
+  if (ensure_smem_attr(kernel, smem, dev, attr_done) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, static_cast<size_t>(smem)) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <typename T, int D>
+int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
+  if (pl.path == DK_PATH_TMA_MMA && fp8) {
+    if constexpr (D >= 128) {
+      using Shape = TmaShapeFp8<D>;
+      static bool attr_done[kMaxDevices] = {false};
+      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true>, Shape::Cfg::kThreads,
+                          Shape::Cfg::kSmemBytes, dev, attr_done);
+    }
+    return 0;
+  }
+  if (pl.path == DK_PATH_TMA_MMA) {
+    using Shape = TmaShape<D>;
+    static bool attr_done[kMaxDevices] = {false};
+    return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps>, Shape::Cfg::kThreads,
+                        Shape::Cfg::kSmemBytes, dev, attr_done);
+  }
+  static bool attr_done[kMaxDevices] = {false};
+  return fp8 ? occupancy_of(paged_decode_simt_kernel<T, D, uint8_t>, kSimtThreads, SimtConfig<D>::kSmemBytes, dev,
+                            attr_done)
+             : occupancy_of(paged_decode_simt_kernel<T, D>, kSimtThreads, SimtConfig<D>::kSmemBytes, dev, attr_done);
+}
+
+int plan_occupancy(const DkPagedAttnArgs& a, const DkPlan& pl, int dev) {
+  if (dev < 0 || pl.path == DK_PATH_NONE) return 0;
+  const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;
+  const bool fp8 = a.kv_fp8 != 0;
+  switch (a.head_dim) {
+    case 64:
+      return bf16 ? partition_occupancy<__nv_bfloat16, 64>(pl, fp8, dev) : partition_occupancy<__half, 64>(pl, fp8, dev);
+    case 128:
+      return bf16 ? partition_occupancy<__nv_bfloat16, 128>(pl, fp8, dev)
+                  : partition_occupancy<__half, 128>(pl, fp8, dev);
+    default:
+      return bf16 ? partition_occupancy<__nv_bfloat16, 256>(pl, fp8, dev)
+                  : partition_occupancy<__half, 256>(pl, fp8, dev);
+  }
 }
 
 template <typename T, int D>
@@ -446,7 +537,22 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
   const dim3 grid(static_cast<unsigned>(pl.num_partitions), static_cast<unsigned>(a.num_kv_heads),
                   static_cast<unsigned>(a.num_seqs));
   cudaError_t e;
-  if (pl.path == DK_PATH_TMA_MMA) {
+  if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
+    if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
+      using Shape = TmaShapeFp8<D>;
+      static bool attr_done[kMaxDevices] = {false};
+      auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true>;
+      const int smem = Shape::Cfg::kSmemBytes;
+      e = ensure_smem_attr(kernel, smem, dev, attr_done);
+      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(fp8 partition kernel)");
+      CUtensorMap kmap, vmap;
+      if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
+      e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
+      if (e != cudaSuccess) return fail_cuda(e, "fp8 partition kernel launch");
+    } else {
+      return fail(1, "internal: fp8 TMA path planned for head_dim %d", D);
+    }
+  } else if (pl.path == DK_PATH_TMA_MMA) {
     using Shape = TmaShape<D>;
     static bool attr_done[kMaxDevices] = {false};
     auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps>;
@@ -457,6 +563,10 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
     if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
     e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
     if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch");
+  } else if (p.kv_fp8) {
+    auto kernel = paged_decode_simt_kernel<T, D, uint8_t>;
+    e = launch_pdl(kernel, grid, dim3(kSimtThreads), SimtConfig<D>::kSmemBytes, stream, p);
+    if (e != cudaSuccess) return fail_cuda(e, "fp8 partition kernel launch (CUDA-core path)");
   } else {
     auto kernel = paged_decode_simt_kernel<T, D>;
     e = launch_pdl(kernel, grid, dim3(kSimtThreads), SimtConfig<D>::kSmemBytes, stream, p);
@@ -507,7 +617,9 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.num_partitions = pl.num_partitions;
   p.ws_partitions = pl.split ? a.max_partitions : 1;
   p.split = pl.split;
-  p.scale_log2 = a.scale * kLog2e;
+  p.kv_fp8 = a.kv_fp8;
+  p.scale_log2 = a.scale * (a.kv_fp8 ? a.k_scale : 1.0f) * kLog2e;
+  p.v_scale = a.kv_fp8 ? a.v_scale : 1.0f;
   const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;
   switch (a.head_dim) {
     case 64:
@@ -751,6 +863,11 @@ int dk_plan(const DkPagedAttnArgs* args, DkPlan* plan) {
     dev = -1;
   }
   dkb::make_plan(*args, dev, plan);
+  int count = 0;
+  if (dev >= 0 && cudaGetDeviceCount(&count) == cudaSuccess && count > 0)
+    plan->ctas_per_sm = dkb::plan_occupancy(*args, *plan, dev);
+  else
+    cudaGetLastError();
   return 0;
 }
 

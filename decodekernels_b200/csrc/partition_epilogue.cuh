@@ -76,7 +76,7 @@ __device__ __forceinline__ void write_merged_result(const DecodeParams& p, float
       e[w] = fast_exp2(red_m[w * kMaxGroup + tid] - M);  // 0 for warps that saw no token
       den = fmaf(e[w], red_l[w * kMaxGroup + tid], den);
     }
-    const float inv = 1.0f / den;
+    const float inv = p.v_scale / den;  // v_scale: V dequantisation factor (1 for 16-bit caches)
 #pragma unroll
     for (int w = 0; w < WARPS; ++w) fac[w * kMaxGroup + tid] = e[w] * inv;
     head[tid] = M;

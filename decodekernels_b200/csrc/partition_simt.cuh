@@ -29,11 +29,18 @@ struct SimtConfig {
   static constexpr int kSmemBytes = RedLayout<D>::floats(kWarps) * 4;
 };
 
-template <typename T, int D>
+// Cache element -> float: the 16-bit types, or e4m3 bytes (exact).
+__device__ __forceinline__ float kv_to_f32(__half x) { return __half2float(x); }
+__device__ __forceinline__ float kv_to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float kv_to_f32(uint8_t x) { return e4m3_to_f32(x); }
+
+// KV: cache element type (T, or uint8_t for e4m3 caches, whose k_scale is in
+// p.scale_log2 and v_scale in the epilogue).
+template <typename T, int D, typename KV = T>
 __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const DecodeParams p) {
   constexpr int V = D / 32;
   constexpr int WARPS = kSimtThreads / 32;
-  using Vec = VecT<T, V>;
+  using Vec = VecT<KV, V>;
   extern __shared__ float simt_smem[];
 
   const int part = blockIdx.x;
@@ -77,8 +84,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     for (int j = 0; j < V; ++j) acc[h][j] = 0.0f;
   }
 
-  const T* kc = static_cast<const T*>(p.k_cache);
-  const T* vc = static_cast<const T*>(p.v_cache);
+  const KV* kc = static_cast<const KV*>(p.k_cache);
+  const KV* vc = static_cast<const KV*>(p.v_cache);
   const int* bt = p.block_tables + static_cast<int64_t>(seq) * p.bt_stride;
   for (int t = pstart + warp; t < pend; t += WARPS) {
     const int lb = t / p.block_size;
@@ -92,8 +99,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
                                                    kv_head * p.v_stride_head + lane * V);
 #pragma unroll
       for (int j = 0; j < V; ++j) {
-        kf[j] = Conv<T>::to_f32(kx.v[j]);
-        vf[j] = Conv<T>::to_f32(vx.v[j]);
+        kf[j] = kv_to_f32(kx.v[j]);
+        vf[j] = kv_to_f32(vx.v[j]);
       }
     } else {  // out-of-range block id: zeros, like the TMA path's out-of-bounds fill
 #pragma unroll

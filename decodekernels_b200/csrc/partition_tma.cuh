@@ -25,22 +25,26 @@
 // * The cross-warp merge and the write-out are in partition_epilogue.cuh.
 #pragma once
 
+#include <type_traits>
+
 #include "decode_params.cuh"
 #include "dk_ptx.cuh"
 #include "partition_epilogue.cuh"
 #include "tile_math.cuh"
+#include "tile_math_fp8.cuh"
 
 namespace dkb {
 
 // WARPS consumer warps of 16 tokens each make a tile of 16 * WARPS tokens
 // (64 for head_dim <= 128, 32 for head_dim 256 so that several CTAs fit on
-// an SM); a tile divides the 64-token partition granularity.
-template <int D, int NSTAGES, int WARPS>
+// an SM); a tile divides the 64-token partition granularity.  KV_BYTES is the
+// cache element size (2, or 1 for e4m3 caches).
+template <int D, int NSTAGES, int WARPS, int KV_BYTES = 2>
 struct TmaConfig {
   static constexpr int kWarps = WARPS;
   static constexpr int kTile = kSubTokens * WARPS;                 // tokens per pipeline stage
   static constexpr int kThreads = (WARPS + 1) * 32;                // + one TMA producer warp
-  static constexpr int kHalves = D / 64;                           // 128-byte column blocks per row
+  static constexpr int kHalves = D * KV_BYTES / 128;               // 128-byte column blocks per row
   static constexpr int kTileBytes = kHalves * kTile * 128;         // K (or V) of one tile
   static constexpr int kStageBytes = 2 * kTileBytes;               // K + V
   static constexpr int kSmemBytes = NSTAGES * kStageBytes + 1024;  // + alignment slack
@@ -51,11 +55,14 @@ struct TmaConfig {
 // Stage layout: page-major.  Page j of a tile (rows = min(block_size, tile)
 // token rows) occupies kPage = 2 * kHalves * rows * 128 bytes: the K column
 // blocks [h][row][128 B] followed by the V column blocks.
-template <typename T, int D, int NSTAGES, int WARPS>
+//
+// FP8: the caches hold e4m3 bytes (rows of D bytes, D / 128 column blocks);
+// the consumers convert in registers (tile_math_fp8.cuh).
+template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false>
 __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap k_map,
                                                                        const __grid_constant__ CUtensorMap v_map,
                                                                        const DecodeParams p) {
-  using Cfg = TmaConfig<D, NSTAGES, WARPS>;
+  using Cfg = TmaConfig<D, NSTAGES, WARPS, FP8 ? 1 : 2>;
   constexpr int TILE = Cfg::kTile;
   constexpr int H = Cfg::kHalves;
 
@@ -156,9 +163,12 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   }
 
   // -------------------------------------------------------------------- consumers
-  WarpAttention<T, D> wa;
+  using Tile = std::conditional_t<FP8, WarpAttentionFp8<T, D>, WarpAttention<T, D>>;
+  Tile wa;
   wa.load_q_global(p, seq, kv_head, lane);
   wa.reset();
+  float scale_log2 = p.scale_log2;
+  if constexpr (FP8) scale_log2 *= wa.q_scale;
   const StageGeom<H> geom(rows_log2);
   const int r0 = warp * kSubTokens;  // first tile row of this warp
   const uint32_t smem_base = smem_u32(smem);
@@ -168,7 +178,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
     const int sub0 = pstart + t * TILE + r0;  // first token of this warp's 16
     if (sub0 < pend) {
       if (!mbar_wait(&full_bar[s], parity)) break;
-      wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, p.scale_log2, lane);
+      wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);

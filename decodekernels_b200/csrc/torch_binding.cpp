@@ -45,10 +45,12 @@ std::string workspace_problem(const at::Tensor& tmp_out, const at::Tensor& max_l
 
 // `partial` non-null: results go to fp32 rows (o, lse, pad) [n, Hq, D + 4]
 // through dk_paged_attention_decode_lse and `out` is not used.
+// k_scale / v_scale: dequantisation factors of e4m3 caches (uint8 or
+// float8_e4m3fn tensors); a cache of q's dtype ignores them.
 void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                  const at::Tensor& block_tables, const at::Tensor& seq_lens, double scale, int64_t max_seq_len,
                  at::Tensor& tmp_out, at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor* merge_counters,
-                 at::Tensor* partial = nullptr) {
+                 at::Tensor* partial = nullptr, double k_scale = 1.0, double v_scale = 1.0) {
   TORCH_CHECK(q.is_cuda(), "paged_attention_decode: q must be a CUDA tensor");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4,
               "k_cache and v_cache must be [num_blocks, block_size, num_kv_heads, head_dim]");
@@ -64,8 +66,18 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
                 "partial must be a contiguous float32 [num_seqs, num_q_heads, head_dim + 4] tensor");
     TORCH_CHECK(partial->device() == q.device(), "partial must be on q's device");
   }
-  check_same(q, k_cache, "q/k_cache");
-  check_same(q, v_cache, "q/v_cache");
+  const auto is_fp8 = [](const at::Tensor& t) {
+    return t.scalar_type() == at::kByte || t.scalar_type() == at::kFloat8_e4m3fn;
+  };
+  const bool kv_fp8 = is_fp8(k_cache);
+  if (kv_fp8) {
+    TORCH_CHECK(is_fp8(v_cache), "k_cache is fp8 (e4m3) but v_cache is ", v_cache.scalar_type());
+    TORCH_CHECK(k_cache.device() == q.device() && v_cache.device() == q.device(),
+                "q/k_cache: tensors must be on the same device");
+  } else {
+    check_same(q, k_cache, "q/k_cache");
+    check_same(q, v_cache, "q/v_cache");
+  }
   TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache shapes differ");
   TORCH_CHECK(q.scalar_type() == at::kHalf || q.scalar_type() == at::kBFloat16,
               "paged_attention_decode: expected float16 or bfloat16, got ", q.scalar_type());
@@ -89,9 +101,10 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
     TORCH_CHECK(k_cache.stride(d) % vec == 0 && v_cache.stride(d) % vec == 0,
                 "KV-cache strides must be multiples of head_dim / 32 for vectorised loads");
   }
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % (vec * 2) == 0 &&
-                  reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % (vec * 2) == 0,
-              "KV-cache pointers must be aligned to head_dim / 16 bytes");
+  const int64_t kv_esz = kv_fp8 ? 1 : 2;
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % (vec * kv_esz) == 0 &&
+                  reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % (vec * kv_esz) == 0,
+              "KV-cache pointers must be aligned to head_dim / 32 elements");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.stride(1) == 1,
               "block_tables must be a 2-D int32 tensor with a contiguous last dimension");
   TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.dim() == 1 && seq_lens.is_contiguous(),
@@ -158,6 +171,9 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
   a.dtype = q.scalar_type() == at::kBFloat16 ? DK_DTYPE_BFLOAT16 : DK_DTYPE_FLOAT16;
   a.flags = 0;
   a.scale = static_cast<float>(scale);
+  a.kv_fp8 = kv_fp8 ? 1 : 0;
+  a.k_scale = static_cast<float>(k_scale);
+  a.v_scale = static_cast<float>(v_scale);
 
   const c10::cuda::OptionalCUDAGuard guard(q.device());
   const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
@@ -191,10 +207,22 @@ void paged_attention_decode_fused(at::Tensor& out, const at::Tensor& q, const at
 void paged_attention_decode_lse(at::Tensor& partial, const at::Tensor& q, const at::Tensor& k_cache,
                                 const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
                                 double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
-                                at::Tensor& exp_sums) {
+                                at::Tensor& exp_sums, double k_scale, double v_scale) {
   at::Tensor unused;
   decode_impl(unused, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
-              nullptr, &partial);
+              nullptr, &partial, k_scale, v_scale);
+}
+
+// Everything of paged_attention_decode plus optional merge counters and the
+// e4m3-cache scales.
+void paged_attention_decode_ext(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache,
+                                const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
+                                double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
+                                at::Tensor& exp_sums, const c10::optional<at::Tensor>& merge_counters, double k_scale,
+                                double v_scale) {
+  at::Tensor counters = merge_counters.has_value() ? *merge_counters : at::Tensor();
+  decode_impl(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+              counters.defined() ? &counters : nullptr, nullptr, k_scale, v_scale);
 }
 
 // Merge partials [R, n, Hq, D + 4] (disjoint token ranges) into out: the
@@ -303,7 +331,12 @@ TORCH_LIBRARY(decode_kernels, m) {
       "Tensor! merge_counters) -> ()");
   m.def(
       "paged_attention_decode_lse(Tensor! partial, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
-      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums) -> ()");
+      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
+      "float k_scale=1.0, float v_scale=1.0) -> ()");
+  m.def(
+      "paged_attention_decode_ext(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
+      "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
+      "Tensor(a!)? merge_counters, float k_scale, float v_scale) -> ()");
   m.def("merge_lse(Tensor! out, Tensor parts) -> ()");
   m.def(
       "reshape_and_cache(Tensor key, Tensor value, Tensor! key_cache, Tensor! value_cache, Tensor slot_mapping, "
@@ -315,5 +348,6 @@ TORCH_LIBRARY_IMPL(decode_kernels, CUDA, m) {
   m.impl("paged_attention_decode_fused", &paged_attention_decode_fused);
   m.impl("reshape_and_cache", &reshape_and_cache);
   m.impl("paged_attention_decode_lse", &paged_attention_decode_lse);
+  m.impl("paged_attention_decode_ext", &paged_attention_decode_ext);
   m.impl("merge_lse", &merge_lse);
 }

@@ -58,7 +58,13 @@ def _register_fakes() -> None:
         return None
 
     @torch.library.register_fake("decode_kernels::paged_attention_decode_lse")
-    def _(partial, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums):
+    def _(partial, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+          k_scale=1.0, v_scale=1.0):
+        return None
+
+    @torch.library.register_fake("decode_kernels::paged_attention_decode_ext")
+    def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
+          merge_counters, k_scale, v_scale):
         return None
 
     @torch.library.register_fake("decode_kernels::merge_lse")
@@ -149,6 +155,8 @@ def paged_attention_decode(
     max_seq_len: int | None = None,
     out: torch.Tensor | None = None,
     workspace: tuple | None = None,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Single-token decode attention over a paged KV cache.
 
@@ -157,6 +165,9 @@ def paged_attention_decode(
     three dims); block_tables: [num_seqs, max_blocks] int32; seq_lens:
     [num_seqs] int32. ``max_seq_len`` must be >= every entry of seq_lens; pass
     it when known to avoid a device-to-host sync.
+
+    Caches of dtype uint8 / float8_e4m3fn hold e4m3 codes (as written by
+    :func:`reshape_and_cache`): K = code * k_scale, V = code * v_scale.
     """
     _require()
     num_seqs, num_q_heads, head_dim = q.shape
@@ -172,10 +183,16 @@ def paged_attention_decode(
         workspace = alloc_workspace(num_seqs, num_q_heads, head_dim, max_seq_len, q.device, num_kv_heads=kv_heads,
                                     block_size=bs)
     tmp_out, max_logits, exp_sums = workspace[:3]
-    if len(workspace) > 3 and workspace[3] is not None:
+    counters = workspace[3] if len(workspace) > 3 else None
+    if k_cache.dtype in (torch.uint8, torch.float8_e4m3fn):
+        torch.ops.decode_kernels.paged_attention_decode_ext(
+            out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits,
+            exp_sums, counters, float(k_scale), float(v_scale)
+        )
+    elif counters is not None:
         torch.ops.decode_kernels.paged_attention_decode_fused(
             out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits,
-            exp_sums, workspace[3]
+            exp_sums, counters
         )
     else:
         torch.ops.decode_kernels.paged_attention_decode(
@@ -210,6 +227,8 @@ def paged_attention_decode_lse(
     max_seq_len: int | None = None,
     partial: torch.Tensor | None = None,
     workspace: tuple | None = None,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Decode attention as fp32 partials: ``[num_seqs, num_q_heads, head_dim + 4]``
     rows holding the normalised output ``o``, then ``lse = log(sum_t exp(scale * q.k_t))``
@@ -235,7 +254,7 @@ def paged_attention_decode_lse(
     tmp_out, max_logits, exp_sums = workspace[:3]
     torch.ops.decode_kernels.paged_attention_decode_lse(partial, q, k_cache, v_cache, block_tables, seq_lens,
                                                         float(scale), int(max_seq_len), tmp_out, max_logits,
-                                                        exp_sums)
+                                                        exp_sums, float(k_scale), float(v_scale))
     return partial
 
 

@@ -199,14 +199,15 @@ class SequenceShardedPagedAttention:
         self._gather_buf = None
 
     def partial(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
-                max_seq_len=None, workspace=None) -> torch.Tensor:
-        """This rank's fp32 partial rows ``[n, Hq, D + 4]`` over its own blocks."""
+                max_seq_len=None, workspace=None, **cache_scales) -> torch.Tensor:
+        """This rank's fp32 partial rows ``[n, Hq, D + 4]`` over its own blocks
+        (``k_scale`` / ``v_scale`` keywords for e4m3 caches)."""
         if scale is None:
             scale = q.shape[-1] ** -0.5
         if max_seq_len is not None:
             max_seq_len = striped_max_len(max_seq_len, self.block_size, self.world)
         return self.lse_fn(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=scale,
-                           max_seq_len=max_seq_len, workspace=workspace)
+                           max_seq_len=max_seq_len, workspace=workspace, **cache_scales)
 
     def gather(self, partial: torch.Tensor) -> torch.Tensor:
         """All-gather every rank's partial into ``[G, n, Hq, D + 4]`` (one
@@ -222,13 +223,15 @@ class SequenceShardedPagedAttention:
         return self._gather_buf
 
     def __call__(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
-                 max_seq_len=None, out=None, workspace=None) -> torch.Tensor:
+                 max_seq_len=None, out=None, workspace=None, k_scale: float = 1.0,
+                 v_scale: float = 1.0) -> torch.Tensor:
         """Full attention output ``[n, Hq, D]`` (q's dtype) on every rank.
 
         ``max_seq_len`` is the longest WHOLE sequence (the local bound is
         derived from it); ``seq_lens_local`` / ``block_tables_local`` are this
         rank's striped lengths and blocks (:func:`stripe_tables`).
         """
+        scales = {} if (k_scale, v_scale) == (1.0, 1.0) else {"k_scale": k_scale, "v_scale": v_scale}
         parts = self.gather(self.partial(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale,
-                                         max_seq_len, workspace))
+                                         max_seq_len, workspace, **scales))
         return self.merge_fn(parts, out=out, dtype=q.dtype)

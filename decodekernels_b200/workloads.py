@@ -35,6 +35,12 @@ class Config:
     layout: str
     sigma: float = 1.0
     pool_blocks: int | None = None  # fixed block pool; None = exactly what the lengths need (+ spare)
+    kv_fp8: bool = False  # caches hold e4m3 codes of the 16-bit draw, x / kv_scale
+    kv_scale: float = 1.0
+
+    @property
+    def kv_bytes_per_elem(self) -> int:
+        return 1 if self.kv_fp8 else torch.finfo(self.dtype).bits // 8
 
 
 CONFIGS = {
@@ -51,8 +57,18 @@ CONFIGS = {
 }
 
 
+# FP8 (e4m3) variants: the same batches with per-tensor-scaled e4m3 caches
+# (as reshape_and_cache writes them), half the KV bytes.
+for _name in ("c2", "c3", "c4", "c5"):
+    _c = CONFIGS[_name]
+    CONFIGS[_name + "f8"] = Config(_name + "f8", _c.description + "; KV cache e4m3 (per-tensor scale 1/64)",
+                                   _c.num_seqs, _c.num_q_heads, _c.num_kv_heads, _c.head_dim, _c.block_size, _c.dtype,
+                                   _c.layout, _c.sigma, _c.pool_blocks, kv_fp8=True, kv_scale=1.0 / 64)
+
+
 def seq_lens(name: str) -> list[int]:
     """The config's lengths, drawn from torch.Generator().manual_seed(0)."""
+    name = name[:-2] if name.endswith("f8") else name
     g = torch.Generator().manual_seed(0)
     if name == "c1":
         return [1, 511, 512, 513]
@@ -87,16 +103,27 @@ class Batch:
 
     def kv_bytes(self) -> int:
         """K+V bytes this batch's call must read: sum L * Hkv_local * D * 2 * esz."""
-        esz = torch.finfo(self.config.dtype).bits // 8
+        esz = self.config.kv_bytes_per_elem
         return sum(self.lens) * self.kv_heads * self.config.head_dim * 2 * esz
 
     def algorithmic_bytes(self) -> int:
         """K+V once + q in + out + block-table entries + seq_lens (int32)."""
         c = self.config
-        esz = torch.finfo(c.dtype).bits // 8
+        esz = torch.finfo(c.dtype).bits // 8  # q and out
         hq = self.q.shape[1]
         tables = sum(-(-L // c.block_size) for L in self.lens) * 4
         return self.kv_bytes() + 2 * len(self.lens) * hq * c.head_dim * esz + tables + 4 * len(self.lens)
+
+
+def _to_e4m3(buf: torch.Tensor, scale: float) -> torch.Tensor:
+    """uint8 e4m3 codes of sat(buf / scale), converted in slices of the first
+    dimension to bound the temporary float32 memory."""
+    out = torch.empty(buf.shape, dtype=torch.uint8, device=buf.device)
+    step = max(1, buf.shape[0] * (64 << 20) // max(buf.numel(), 1))
+    for i in range(0, buf.shape[0], step):
+        x = buf[i : i + step].float().div_(scale).clamp_(-448.0, 448.0)
+        out[i : i + step] = x.to(torch.float8_e4m3fn).view(torch.uint8)
+    return out
 
 
 def _layout_views(buf: torch.Tensor, layout: str, head_dim: int):
@@ -139,6 +166,8 @@ def make_striped(name: str, device="cuda", stripe: tuple[int, int] = (0, 1), see
         buf = torch.randn(2, pool, bs, hkv, d, generator=gen, device=device, dtype=c.dtype)
     if c.sigma != 1.0:
         buf.mul_(c.sigma)
+    if c.kv_fp8:
+        buf = _to_e4m3(buf, c.kv_scale)
     k, v = _layout_views(buf, c.layout, d)
     perm = torch.randperm(pool, generator=torch.Generator().manual_seed(seed + 7 + rank)).to(torch.int32)
     width = max(max(mine) if mine else 1, 1)
@@ -187,6 +216,8 @@ def make(name: str, device="cuda", shard: tuple[int, int] = (0, 1), seed: int = 
         buf = torch.randn(2, pool, bs, hkv, d, generator=gen, device=device, dtype=c.dtype)
     if c.sigma != 1.0:
         buf.mul_(c.sigma)
+    if c.kv_fp8:
+        buf = _to_e4m3(buf, c.kv_scale)
     k, v = _layout_views(buf, c.layout, d)
     perm = torch.randperm(pool, generator=torch.Generator().manual_seed(seed + 7)).to(torch.int32)
     width = max(max(nblk) if nblk else 1, 1)
@@ -225,3 +256,16 @@ def compact_sequences(batch: Batch, seqs: list[int]):
             tables[i, : len(r)] = torch.tensor(r, dtype=torch.int32)
     lens = torch.tensor([batch.lens[s] for s in seqs], dtype=torch.int32)
     return batch.q[seqs].cpu(), PagedKV(k, v, tables, lens, bs)
+
+
+def dequantize(kv: PagedKV, config: Config) -> PagedKV:
+    """For an e4m3 config, the same cache as ``config.dtype`` values
+    (code * kv_scale; exact for the power-of-two scale used here), e.g. to
+    check a batch against a 16-bit reference; other configs unchanged."""
+    if not config.kv_fp8:
+        return kv
+
+    def deq(c):
+        return (c.view(torch.float8_e4m3fn).to(torch.float32) * config.kv_scale).to(config.dtype)
+
+    return PagedKV(deq(kv.k_cache), deq(kv.v_cache), kv.block_tables, kv.seq_lens, kv.block_size)

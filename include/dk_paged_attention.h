@@ -116,6 +116,9 @@ typedef struct DkPagedAttnArgs {
   int32_t dtype;          /* DK_DTYPE_* */
   int32_t flags;          /* DK_FLAG_* */
   float scale;            /* softmax scale, usually head_dim ** -0.5 */
+  int32_t kv_fp8;         /* 1: the caches hold e4m3 bytes (K = code * k_scale, V = code * v_scale); strides and
+                             alignment rules are then in bytes.  0: the caches have q's dtype */
+  float k_scale, v_scale; /* FP8 caches only: positive, finite per-tensor scales */
 } DkPagedAttnArgs;
 
 /* The launch a call would make. */
@@ -128,6 +131,7 @@ typedef struct DkPlan {
   int32_t stages;         /* shared-memory pipeline depth of the TMA path */
   int32_t smem_bytes;     /* dynamic shared memory of the partition kernel */
   int32_t launches;       /* kernels launched by one call (1 or 2; 1 with merge counters) */
+  int32_t ctas_per_sm;    /* resident partition-kernel CTAs per SM (occupancy query; 0 without a GPU) */
 } DkPlan;
 
 /*

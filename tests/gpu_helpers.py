@@ -83,3 +83,33 @@ def assert_workspace_matches(ws, kv, q, partition_size, scale=None, what=""):
         np.testing.assert_allclose(ml[s, :, :live], m_ref[s, :, :live], atol=2e-2, rtol=1e-2, err_msg=f"{what} m")
         np.testing.assert_allclose(es[s, :, :live], s_ref[s, :, :live], atol=2e-2, rtol=2e-2, err_msg=f"{what} s")
         np.testing.assert_allclose(tmp[s, :, :live], o_ref[s, :, :live], atol=2e-2, rtol=2e-2, err_msg=f"{what} o")
+
+
+def fp8_caches(kv, layout, k_scale, v_scale):
+    """e4m3 copies (uint8) of a 16-bit paged cache in the same layout -- one
+    interleaved K|V buffer for the "vllm" layout, so the fused TMA map is used
+    -- quantised as sat_e4m3(x / scale)."""
+    nb, bs, h, d = kv.k_cache.shape
+    if layout == "vllm":
+        buf = torch.empty(nb, h, bs, 2 * d, dtype=torch.uint8, device=kv.k_cache.device)
+        k8, v8 = buf.transpose(1, 2).split(d, dim=-1)
+    elif layout == "hnd":
+        k8 = torch.empty(nb, h, bs, d, dtype=torch.uint8, device=kv.k_cache.device).transpose(1, 2)
+        v8 = torch.empty(nb, h, bs, d, dtype=torch.uint8, device=kv.k_cache.device).transpose(1, 2)
+    else:
+        k8 = torch.empty(nb, bs, h, d, dtype=torch.uint8, device=kv.k_cache.device)
+        v8 = torch.empty_like(k8)
+    for dst, src, s in ((k8, kv.k_cache, k_scale), (v8, kv.v_cache, v_scale)):
+        q8 = (src.float() / s).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+        dst.copy_(q8)
+    return k8, v8
+
+
+def oracle_dense_fp8(q, kv, k8, v8, k_scale, v_scale, scale=None):
+    """The oracle on the dequantised e4m3 caches (code * scale)."""
+    from oracle import cache_write as cw
+
+    kd = cw.e4m3_decode(k8.cpu().numpy()) * np.float32(k_scale)
+    vd = cw.e4m3_decode(v8.cpu().numpy()) * np.float32(v_scale)
+    return oracle.paged_attention_dense(q.cpu(), kd, vd, kv.block_tables.cpu().numpy(), kv.seq_lens.cpu().numpy(),
+                                        scale=scale)

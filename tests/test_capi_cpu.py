@@ -32,15 +32,15 @@ def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (dk_\w+)", out))
     assert set(_declared()) <= exported
-    assert capi.version() == 400
+    assert capi.version() == 500
 
 
 def test_struct_layout_matches_header(tmp_path):
     """The ctypes mirrors have the C compiler's size and field offsets for
     include/dk_paged_attention.h."""
-    # 10 pointers + 11 int64 + 11 int32 + 1 float = 216 bytes, no padding surprises
-    assert ctypes.sizeof(capi.DkPagedAttnArgs) == 216
-    assert ctypes.sizeof(capi.DkPlan) == 32
+    # 10 pointers + 11 int64 + 12 int32 + 3 float = 228 bytes, padded to 232 (8-byte alignment)
+    assert ctypes.sizeof(capi.DkPagedAttnArgs) == 232
+    assert ctypes.sizeof(capi.DkPlan) == 36
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dk_paged_attention.h"', "int main(void) {"]
     structs = (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan),
                ("DkCacheWriteArgs", capi.DkCacheWriteArgs), ("DkLseMergeArgs", capi.DkLseMergeArgs))
@@ -174,6 +174,26 @@ def test_misaligned_workspace_is_rejected():
     a = _args(max_seq_len=3000, ws=_ws(4, 32, 47))
     a.tmp_out += 4
     assert _plan(a)[0] == 1 and "16-byte aligned" in capi.last_error()
+
+
+def test_fp8_caches_plan_and_validate():
+    kv8 = torch.zeros(64, 16, 8, 128, dtype=torch.uint8)
+    q = torch.zeros(4, 32, 128, dtype=torch.bfloat16)
+    bt = torch.zeros(4, 64, dtype=torch.int32)
+    sl = torch.zeros(4, dtype=torch.int32)
+    a = capi.make_args(q, kv8, kv8, bt, sl, 128**-0.5, 3000, q, _ws(4, 32, 47), 0, False, 0, 0.5, 0.25)
+    assert a.kv_fp8 == 1 and a.k_scale == 0.5
+    rc, p = _plan(a)
+    assert rc == 0 and p["path"] == capi.DK_PATH_TMA_MMA and p["stages"] == 4
+    # e4m3 rows of 64 bytes go to the CUDA-core path
+    kv64 = torch.zeros(64, 16, 8, 64, dtype=torch.uint8)
+    q64 = torch.zeros(4, 32, 64, dtype=torch.bfloat16)
+    rc, p = _plan(capi.make_args(q64, kv64, kv64, bt, sl, 0.125, 3000, q64, None, 0, False, 0, 1.0, 1.0))
+    assert rc == 0 and p["path"] == capi.DK_PATH_SIMT
+    a.v_scale = 0.0
+    assert _plan(a)[0] == 1 and "k_scale and v_scale" in capi.last_error()
+    a.v_scale, a.kv_fp8 = 1.0, 3
+    assert _plan(a)[0] == 1 and "kv_fp8" in capi.last_error()
 
 
 def test_plan_fixed_partition_size():
