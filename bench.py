@@ -283,7 +283,8 @@ def run_gpu_arm(args) -> None:
         from decodekernels_b200.sharded import SequenceShardedPagedAttention, striped_max_len
 
         batch = workloads.make_striped(args.workload, dev, stripe=(rank, world))
-        seq_attn = SequenceShardedPagedAttention(block_size=batch.config.block_size, rank=rank, world=world)
+        seq_attn = SequenceShardedPagedAttention(block_size=batch.config.block_size, rank=rank, world=world,
+                                                 exchange=args.exchange)
         full_max = max(workloads.seq_lens(args.workload))
         max_len = striped_max_len(full_max, batch.config.block_size, world)
     else:
@@ -453,8 +454,10 @@ def run_gpu_arm(args) -> None:
                 "num_seqs": n, "num_q_heads": batch.config.num_q_heads, "num_kv_heads": batch.config.num_kv_heads,
                 "head_dim": d, "block_size": kv.block_size, "max_seq_len": max_len,
                 "kv_bytes_total": kv_total, "algorithmic_bytes_total": alg_total,
-                "parallelism": (f"sequence shard (block-striped) x{world}, NCCL all-gather of partials + "
-                                "LSE merge in every step" if seq_mode else f"kv-head shard x{world}")
+                "parallelism": ((f"sequence shard (block-striped) x{world}, partials pushed to every GPU over "
+                                 "NVLink peer memory + LSE merge in one kernel every step" if args.exchange == "p2p"
+                                 else f"sequence shard (block-striped) x{world}, NCCL all-gather of partials + "
+                                      "LSE merge in every step") if seq_mode else f"kv-head shard x{world}")
                                if world > 1 else "single GPU",
                 "l2": "L2 flushed (256 MB write) before every step" if flush else
                       "inputs larger than L2 (no flush between steps)",
@@ -470,6 +473,7 @@ def run_gpu_arm(args) -> None:
             "e2e": {"value": kv_total / (e2e_s / e_steps) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e_steps, "api": "decodekernels_b200.paged_attention_decode"},
             "gpu_launches": args.steps * (plan["launches"] + (1 if seq_mode else 0)),
+            "exchange_errors": seq_attn.p2p_errors() if seq_mode else None,
             "with_gather": None if not gather_s else {
                 "us_per_call": gather_s / args.steps * 1e6, "value": kv_total / (gather_s / args.steps) / 1e12,
                 "unit": UNIT, "note": "decode + NCCL all-gather of the per-head outputs to every rank"},
@@ -495,6 +499,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c5",
                     choices=["c1", "c2", "c3", "c4", "c5", "c2f8", "c3f8", "c4f8", "c5f8"])
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="sequence sharding: partial rows pushed over NVLink peer memory (one kernel) or an NCCL "
+                         "all-gather followed by the merge kernel")
     ap.add_argument("--sharding", default="auto", choices=["auto", "head", "seq"],
                     help="N>1: KV-head sharding (no exchange) or block-striped sequence sharding (partials "
                          "all-gathered and merged every step); auto = head when the KV heads divide evenly")

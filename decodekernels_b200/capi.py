@@ -32,7 +32,7 @@ DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
             "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache",
-            "dk_paged_attention_decode_lse", "dk_merge_lse")
+            "dk_paged_attention_decode_lse", "dk_merge_lse", "dk_exchange_merge_lse")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -121,6 +121,28 @@ class DkLseMergeArgs(ctypes.Structure):
     ]
 
 
+DK_MAX_PEERS = 8
+
+
+class DkPeerExchangeArgs(ctypes.Structure):
+    _fields_ = [
+        ("partial", ctypes.c_void_p),
+        ("recv", ctypes.c_void_p * DK_MAX_PEERS),
+        ("flags", ctypes.c_void_p * DK_MAX_PEERS),
+        ("state", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_stride_seq", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("num_seqs", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("wait_limit_ms", ctypes.c_uint32),
+    ]
+
+
 class DkPlan(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int32),
@@ -172,6 +194,8 @@ def load() -> ctypes.CDLL:
         lib.dk_paged_attention_decode_lse.restype = ctypes.c_int
         lib.dk_merge_lse.argtypes = [ctypes.POINTER(DkLseMergeArgs), ctypes.c_void_p]
         lib.dk_merge_lse.restype = ctypes.c_int
+        lib.dk_exchange_merge_lse.argtypes = [ctypes.POINTER(DkPeerExchangeArgs), ctypes.c_void_p]
+        lib.dk_exchange_merge_lse.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -378,4 +402,29 @@ def merge_lse(parts, out, stream=None) -> int:
     rc = load().dk_merge_lse(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_merge_lse failed ({rc}): {last_error()}")
+    return rc
+
+
+def exchange_merge_lse(partial, recv_ptrs, flag_ptrs, state, out, rank: int, world: int, wait_limit_ms: int = 0,
+                       stream=None) -> int:
+    """dk_exchange_merge_lse: push ``partial`` [n, Hq, D + 4] to every GPU's
+    receive buffer, wait for every rank's flag, merge into ``out`` [n, Hq, D]."""
+    import torch
+
+    a = DkPeerExchangeArgs()
+    a.partial = partial.data_ptr()
+    for r in range(world):
+        a.recv[r] = recv_ptrs[r]
+        a.flags[r] = flag_ptrs[r]
+    a.state = state.data_ptr()
+    a.out, a.out_stride_seq, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.rank, a.world = rank, world
+    a.num_seqs, a.num_q_heads, a.head_dim = partial.shape[0], partial.shape[1], partial.shape[2] - 4
+    a.dtype = _dtype_code(out)
+    a.wait_limit_ms = wait_limit_ms
+    if stream is None:
+        stream = torch.cuda.current_stream(partial.device).cuda_stream
+    rc = load().dk_exchange_merge_lse(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_exchange_merge_lse failed ({rc}): {last_error()}")
     return rc

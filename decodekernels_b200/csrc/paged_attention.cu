@@ -23,12 +23,13 @@
 #include "merge_partitions.cuh"
 #include "partition_simt.cuh"
 #include "partition_tma.cuh"
+#include "peer_exchange.cuh"
 #include "reshape_and_cache.cuh"
 
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 500;  // 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
+constexpr int kVersion = 600;  // 0.6.0: dk_exchange_merge_lse; 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
                                 // dk_paged_attention_decode_lse / dk_merge_lse; 0.3.0: dk_reshape_and_cache;
                                 // 0.2.0: DkPagedAttnArgs.merge_counters
 // Planner: partitions are sized so that the grid is about one wave of
@@ -713,6 +714,60 @@ int launch_lse_merge(const DkLseMergeArgs& a, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------------------
+// Peer-memory exchange of sequence-shard partials
+// ---------------------------------------------------------------------------
+int validate_peer_exchange(const DkPeerExchangeArgs* a) {
+  if (a == nullptr) return fail(1, "dk_exchange_merge_lse: args is NULL");
+  if (a->world < 1 || a->world > DK_MAX_PEERS || a->rank < 0 || a->rank >= a->world)
+    return fail(1, "dk_exchange_merge_lse: need 0 <= rank < world <= %d", DK_MAX_PEERS);
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(1, "head_dim must be 64, 128 or 256, got %d", a->head_dim);
+  if (a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
+    return fail(1, "dk_exchange_merge_lse: out must be float16 or bfloat16 (dtype code %d)", a->dtype);
+  if (a->num_seqs < 0 || a->num_q_heads <= 0) return fail(1, "dk_exchange_merge_lse: bad sizes");
+  if (!a->partial || !a->state || !a->out) return fail(1, "dk_exchange_merge_lse: NULL pointer");
+  if (!aligned(a->partial, 16)) return fail(1, "dk_exchange_merge_lse: partial must be 16-byte aligned");
+  for (int r = 0; r < a->world; ++r) {
+    if (!a->recv[r] || !a->flags[r]) return fail(1, "dk_exchange_merge_lse: NULL peer pointer for rank %d", r);
+    if (!aligned(a->recv[r], 16) || !aligned(a->flags[r], 4))
+      return fail(1, "dk_exchange_merge_lse: receive buffers must be 16-byte aligned");
+  }
+  return 0;
+}
+
+template <int D>
+int launch_peer_exchange(const DkPeerExchangeArgs& a, int dev, cudaStream_t stream) {
+  PeerExchangeParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.partial = a.partial;
+  for (int r = 0; r < a.world; ++r) {
+    p.recv[r] = a.recv[r];
+    p.flags[r] = a.flags[r];
+  }
+  p.state = a.state;
+  p.out = a.out;
+  p.out_stride_seq = a.out_stride_seq;
+  p.out_stride_head = a.out_stride_head;
+  p.block_floats = static_cast<int64_t>(a.num_seqs) * a.num_q_heads * (D + 4);
+  p.rank = a.rank;
+  p.world = a.world;
+  p.num_seqs = a.num_seqs;
+  p.num_q_heads = a.num_q_heads;
+  p.wait_limit_ns = (a.wait_limit_ms ? a.wait_limit_ms : 2000u) * 1000000ull;
+  // at most two CTAs per SM: every CTA must be resident while they wait on one another's flags
+  const long long pairs = static_cast<long long>(a.num_seqs) * a.num_q_heads;
+  const long long want = std::max<long long>(std::max<long long>(1, (pairs + 7) / 8),
+                                             (p.block_floats / 4 + kExchangeThreads - 1) / kExchangeThreads);
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(want, 2LL * num_sms(dev))));
+  if (a.dtype == DK_DTYPE_BFLOAT16)
+    peer_exchange_merge_kernel<__nv_bfloat16, D><<<grid, kExchangeThreads, 0, stream>>>(p);
+  else
+    peer_exchange_merge_kernel<__half, D><<<grid, kExchangeThreads, 0, stream>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail_cuda(e, "peer exchange kernel launch");
+}
+
+// ---------------------------------------------------------------------------
 // Paged-KV write
 // ---------------------------------------------------------------------------
 int validate_cache_write(const DkCacheWriteArgs* a) {
@@ -916,6 +971,22 @@ int dk_merge_lse(const DkLseMergeArgs* args, dk_stream_t stream) {
       return dkb::launch_lse_merge<128>(*args, s);
     default:
       return dkb::launch_lse_merge<256>(*args, s);
+  }
+}
+
+int dk_exchange_merge_lse(const DkPeerExchangeArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate_peer_exchange(args)) return e;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (args->head_dim) {
+    case 64:
+      return dkb::launch_peer_exchange<64>(*args, dev, s);
+    case 128:
+      return dkb::launch_peer_exchange<128>(*args, dev, s);
+    default:
+      return dkb::launch_peer_exchange<256>(*args, dev, s);
   }
 }
 

@@ -1,0 +1,153 @@
+// Exchange and merge of sequence-shard partials over NVLink peer memory, in
+// one kernel per GPU (the collective the NCCL all-gather does, without a
+// library round trip).  Each GPU holds, in memory every peer can address
+// (symmetric allocations), a flag per rank and two receive buffers of
+// R partial blocks [n, Hq, D + 4].  Call number e (kept on the device, so a
+// captured CUDA graph replays correctly) runs, on every GPU:
+//
+//   1. push: copy this GPU's partial rows into slot (e % 2, rank) of every
+//      GPU's receive buffer (peer stores over NVLink, 16 bytes at a time);
+//   2. publish: every CTA counts itself done after a GPU-scope release of its
+//      stores; the last one fences at system scope and stores e into this
+//      rank's flag on every GPU (release, system scope);
+//   3. wait: every CTA spins (bounded by wait_limit_ns of %globaltimer, then
+//      it records the give-up in the error word and carries on) until every
+//      rank's flag on this GPU has reached e (acquire, system scope);
+//   4. merge: the log-sum-exp merge of the R local slots into `out`;
+//   5. the last CTA to finish advances the call counter.
+//
+// Two receive buffers suffice: a GPU can push call e + 1 only after its merge
+// of call e, which needed every peer's flag e, which each peer set only after
+// its own merge of call e - 1 -- so slot (e + 1) % 2 is no longer read.
+// The grid is at most a few CTAs per SM so that every CTA is resident while
+// they wait.  No TMA and no multicast: plain 16-byte peer loads and stores.
+#pragma once
+
+#include "decode_params.cuh"
+#include "dk_ptx.cuh"
+
+namespace dkb {
+
+constexpr int kMaxPeers = 8;
+constexpr int kExchangeThreads = 256;
+
+struct PeerExchangeParams {
+  const float* partial;          // this GPU's rows [n, Hq, D + 4]
+  float* recv[kMaxPeers];        // every GPU's receive buffers [2][R][n * Hq * (D + 4)]
+  uint32_t* flags[kMaxPeers];    // every GPU's flag words [R]
+  uint32_t* state;               // this GPU: [0] completed calls, [1] pushers done, [2] mergers done, [3] errors
+  void* out;                     // [n, Hq, D] of T, strided
+  int64_t out_stride_seq, out_stride_head;
+  int64_t block_floats;          // n * Hq * (D + 4)
+  int rank, world, num_seqs, num_q_heads;
+  unsigned long long wait_limit_ns;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kExchangeThreads) peer_exchange_merge_kernel(const PeerExchangeParams p) {
+  constexpr int ROW = D + 4;
+  constexpr int V = D / 32;
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_last;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_epoch = p.state[0] + 1;  // nothing advances state[0] before every CTA has merged
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int par = static_cast<int>(e & 1u);
+
+  // 1. push this GPU's rows into slot (par, rank) of every GPU
+  const int64_t n4 = p.block_floats / 4;
+  const float4* src = reinterpret_cast<const float4*>(p.partial);
+  const int64_t slot = (static_cast<int64_t>(par) * p.world + p.rank) * p.block_floats;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExchangeThreads + tid; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * kExchangeThreads) {
+    const float4 v = src[i];
+    for (int r = 0; r < p.world; ++r) reinterpret_cast<float4*>(p.recv[r] + slot)[i] = v;
+  }
+  // 2. publish: the last CTA to finish pushing sets this rank's flag everywhere
+#ifndef DK_PEER_FENCE_EACH_THREAD
+  // The CTA barrier orders every thread's stores before thread 0's
+  // GPU-scope release; the last CTA acquires all of them through the counter
+  // and its system-scope release of the flags is cumulative over them.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&p.state[1], 1u) == gridDim.x - 1;
+  }
+#else
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.state[1], 1u) == gridDim.x - 1;
+#endif
+  __syncthreads();
+  if (s_last) {
+    if (tid == 0) __threadfence_system();
+    __syncthreads();
+    if (tid < p.world) st_release_sys(p.flags[tid] + p.rank, e);
+    if (tid == 0) p.state[1] = 0;
+  }
+  // 3. wait for every rank's flag on this GPU
+  if (tid == 0) {
+    const unsigned long long t0 = global_timer_ns();
+    for (int r = 0; r < p.world; ++r) {
+      while (static_cast<int32_t>(ld_acquire_sys(p.flags[p.rank] + r) - e) < 0) {
+        if (global_timer_ns() - t0 > p.wait_limit_ns) {
+          atomicAdd(&p.state[3], 1u);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // 4. merge the R slots, one warp per (seq, q_head)
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const float* base = p.recv[p.rank] + static_cast<int64_t>(par) * p.world * p.block_floats;
+  const int64_t pairs = static_cast<int64_t>(p.num_seqs) * p.num_q_heads;
+  for (int64_t pair = static_cast<int64_t>(blockIdx.x) * (kExchangeThreads / 32) + warp; pair < pairs;
+       pair += static_cast<int64_t>(gridDim.x) * (kExchangeThreads / 32)) {
+    const float* rows = base + pair * ROW;
+    float m = -INFINITY;
+    for (int r = lane; r < p.world; r += 32) m = fmaxf(m, __ldcg(rows + r * p.block_floats + D));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float acc[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = 0.0f;
+    float sum = 0.0f;
+    if (m != -INFINITY) {
+      for (int r = 0; r < p.world; ++r) {
+        const float* row = rows + r * p.block_floats;
+        const float w = fast_exp2((__ldcg(row + D) - m) * kLog2e);
+        sum += w;
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc[j] = fmaf(w, __ldcg(row + lane * V + j), acc[j]);
+      }
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+    const int seq = static_cast<int>(pair / p.num_q_heads);
+    const int q_head = static_cast<int>(pair - static_cast<int64_t>(seq) * p.num_q_heads);
+    T* dst = static_cast<T*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head + lane * V;
+#pragma unroll
+    for (int j = 0; j < V; ++j) dst[j] = Conv<T>::from_f32(acc[j] * inv);
+  }
+  // 5. the last CTA to finish advances the call counter
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&p.state[2], 1u) == gridDim.x - 1) {
+    p.state[2] = 0;
+    p.state[0] = e;
+  }
+}
+
+}  // namespace dkb

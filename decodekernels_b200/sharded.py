@@ -179,7 +179,8 @@ class SequenceShardedPagedAttention:
     """
 
     def __init__(self, block_size: int, rank: int | None = None, world: int | None = None, group=None,
-                 lse_fn: Callable | None = None, merge_fn: Callable | None = None):
+                 lse_fn: Callable | None = None, merge_fn: Callable | None = None, exchange: str = "nccl",
+                 wait_limit_ms: int = 0):
         import torch.distributed as dist
 
         if rank is None or world is None:
@@ -197,6 +198,11 @@ class SequenceShardedPagedAttention:
             merge_fn = merge_fn or merge_lse
         self.lse_fn, self.merge_fn = lse_fn, merge_fn
         self._gather_buf = None
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', got {exchange!r}")
+        self.exchange = exchange
+        self.wait_limit_ms = wait_limit_ms
+        self._p2p = None  # (block_floats, symmetric buffer, handle, recv ptrs, flag ptrs, state)
 
     def partial(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
                 max_seq_len=None, workspace=None, **cache_scales) -> torch.Tensor:
@@ -222,6 +228,34 @@ class SequenceShardedPagedAttention:
         dist.all_gather_into_tensor(self._gather_buf.view(-1), partial.contiguous().view(-1), group=self.group)
         return self._gather_buf
 
+    # ------------------------------------------------------------ peer memory
+    _FLAG_FLOATS = 64  # flag words at the head of each rank's symmetric buffer (256 bytes)
+
+    def _p2p_buffers(self, block_floats: int, device):
+        """Symmetric allocation (collective on first use, or when a larger batch
+        needs more room): every rank's [flags | 2 x world receive blocks]."""
+        if self._p2p is not None and self._p2p[0] >= block_floats:
+            return self._p2p
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        group = self.group if self.group is not None else dist.group.WORLD
+        buf = symm.empty(self._FLAG_FLOATS + 2 * self.world * block_floats, dtype=torch.float32, device=device)
+        buf.zero_()
+        hdl = symm.rendezvous(buf, group)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        base = [int(x) for x in hdl.buffer_ptrs]
+        flags = [b for b in base]
+        recv = [b + 4 * self._FLAG_FLOATS for b in base]
+        state = torch.zeros(4, dtype=torch.int32, device=device)
+        self._p2p = (block_floats, buf, hdl, recv, flags, state)
+        return self._p2p
+
+    def p2p_errors(self) -> int:
+        """Peer waits that gave up (state word 3) since the buffers were made."""
+        return 0 if self._p2p is None else int(self._p2p[5][3].item())
+
     def __call__(self, q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale=None,
                  max_seq_len=None, out=None, workspace=None, k_scale: float = 1.0,
                  v_scale: float = 1.0) -> torch.Tensor:
@@ -232,6 +266,15 @@ class SequenceShardedPagedAttention:
         rank's striped lengths and blocks (:func:`stripe_tables`).
         """
         scales = {} if (k_scale, v_scale) == (1.0, 1.0) else {"k_scale": k_scale, "v_scale": v_scale}
-        parts = self.gather(self.partial(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale,
-                                         max_seq_len, workspace, **scales))
-        return self.merge_fn(parts, out=out, dtype=q.dtype)
+        partial = self.partial(q, k_cache_local, v_cache_local, block_tables_local, seq_lens_local, scale,
+                               max_seq_len, workspace, **scales)
+        if self.exchange == "p2p" and self.world > 1:
+            from . import capi
+
+            n, hq, row = partial.shape
+            _, _, _, recv, flags, state = self._p2p_buffers(n * hq * row, partial.device)
+            if out is None:
+                out = torch.empty(n, hq, row - 4, dtype=q.dtype, device=q.device)
+            capi.exchange_merge_lse(partial, recv, flags, state, out, self.rank, self.world, self.wait_limit_ms)
+            return out
+        return self.merge_fn(self.gather(partial), out=out, dtype=q.dtype)

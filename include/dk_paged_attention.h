@@ -211,6 +211,39 @@ typedef struct DkLseMergeArgs {
 DK_API int dk_merge_lse(const DkLseMergeArgs* args, dk_stream_t stream);
 
 /*
+ * Exchange of sequence-shard partials over NVLink peer memory plus the merge,
+ * in one kernel per GPU: the alternative to an NCCL all-gather followed by
+ * dk_merge_lse.  Every GPU of the group calls it once per decode step, after
+ * its dk_paged_attention_decode_lse, with the same sizes.  Memory (allocated
+ * by the caller so that every GPU can address every other GPU's copy, e.g.
+ * with torch.distributed symmetric memory):
+ *   recv[r]   float [2][world][num_seqs * num_q_heads * (head_dim + 4)] on GPU r
+ *   flags[r]  uint32 [world] on GPU r, zero before the first call
+ *   state     uint32 [4] on this GPU, zero before the first call
+ * The call copies `partial` into slot (call parity, rank) of every GPU's
+ * receive buffer, publishes its flag on every GPU, waits (bounded by
+ * wait_limit_ms; a give-up adds 1 to state[3] and the call goes on) until
+ * every rank's flag has reached this call's number, and merges the world
+ * slots into out [num_seqs, num_q_heads, head_dim].  The call counter lives
+ * in `state`, so a captured CUDA graph replays correctly.  Concurrent calls
+ * on one group need separate buffers.  world <= DK_MAX_PEERS.
+ */
+#define DK_MAX_PEERS 8
+typedef struct DkPeerExchangeArgs {
+  const float* partial;            /* this GPU's rows [num_seqs, num_q_heads, head_dim + 4] */
+  float* recv[DK_MAX_PEERS];       /* receive buffers of ranks 0..world-1 as this GPU addresses them */
+  uint32_t* flags[DK_MAX_PEERS];   /* flag words of ranks 0..world-1 as this GPU addresses them */
+  uint32_t* state;
+  void* out;
+  int64_t out_stride_seq, out_stride_head;
+  int32_t rank, world, num_seqs, num_q_heads, head_dim;
+  int32_t dtype;                   /* DK_DTYPE_FLOAT16 / DK_DTYPE_BFLOAT16 of out */
+  uint32_t wait_limit_ms;          /* 0: 2000 */
+} DkPeerExchangeArgs;
+
+DK_API int dk_exchange_merge_lse(const DkPeerExchangeArgs* args, dk_stream_t stream);
+
+/*
  * Paged-KV write, the step before decode: no counterpart in DecodeKernels
  * (its decode reads caches that vLLM's reshape_and_cache_flash wrote); this
  * is that operation.  For every token t with slot = slot_mapping[t] in

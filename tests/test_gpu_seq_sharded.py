@@ -185,3 +185,103 @@ def test_two_nccl_ranks_exchange_partials():
                        capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("ok") == 2
+
+
+def test_peer_exchange_wait_gives_up_and_reports():
+    """One GPU, world 2: the second rank's flag is a word nothing sets, so the
+    exchange's bounded wait runs out, records the give-up in state[3] and
+    returns; the context stays usable."""
+    n, hq, d = 3, 8, 128
+    partial = torch.zeros(n, hq, d + 4, device="cuda")
+    partial[..., d] = 0.0
+    block = n * hq * (d + 4)
+    mine = torch.zeros(64 + 2 * 2 * block, device="cuda")
+    other = torch.zeros_like(mine)  # stands in for a peer that never calls
+    recv = [mine.data_ptr() + 256, other.data_ptr() + 256]
+    flags = [mine.data_ptr(), other.data_ptr()]
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")
+    out = torch.empty(n, hq, d, dtype=torch.bfloat16, device="cuda")
+    capi.exchange_merge_lse(partial, recv, flags, state, out, rank=0, world=2, wait_limit_ms=100)
+    torch.cuda.synchronize()
+    assert int(state[3].item()) >= 1  # gave up instead of hanging
+    other_flags = other.view(torch.int32)
+    assert int(other_flags[0].item()) == 1 and int(other_flags[1].item()) == 0  # we signalled; the peer never did
+    kv = make_paged_kv([100], 1, 128, 16, torch.bfloat16, "cuda")
+    q = _q(1, 8, 128, torch.bfloat16)
+    assert_attention_close(dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens),
+                           oracle_dense(q, kv), torch.bfloat16, "after a given-up exchange")
+
+
+_P2P_SCRIPT = textwrap.dedent(
+    """
+    import datetime, os, sys
+    sys.path.insert(0, {root!r}); sys.path.insert(0, {tests!r})
+    import torch, torch.distributed as dist
+    from decodekernels_b200.sharded import SequenceShardedPagedAttention, stripe_tables
+    from decodekernels_b200.testing import make_paged_kv
+    from gpu_helpers import assert_attention_close, oracle_dense
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    L = 4000
+    lens0 = [7, 900, L, 64, 0, 1500]
+    full = make_paged_kv([L] * len(lens0), 2, 128, 16, torch.bfloat16, "cpu", layout="nhd", seed=31)
+    q_cpu = torch.randn(len(lens0), 16, 128, generator=torch.Generator().manual_seed(32), dtype=torch.bfloat16)
+    q = q_cpu.cuda()
+    attn = SequenceShardedPagedAttention(block_size=16, exchange="p2p")
+    nccl = SequenceShardedPagedAttention(block_size=16)
+    k, v = full.k_cache.cuda(), full.v_cache.cuda()  # whole cache here; each rank reads only its blocks
+    bt_full = full.block_tables.cuda()
+    lens = torch.tensor(lens0, dtype=torch.int32, device="cuda")
+    out = torch.empty(len(lens0), 16, 128, dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        bt, ll = stripe_tables(bt_full, lens, 16, attn.rank, attn.world)
+        attn(q, k, v, bt, ll, max_seq_len=L, out=out)
+
+    g = torch.Generator().manual_seed(33)
+    for it in range(4):  # eager calls: the device-side call counter advances in lockstep
+        lens.copy_(torch.randint(0, L + 1, (len(lens0),), generator=g, dtype=torch.int32))
+        step()
+        torch.cuda.synchronize()
+        full.seq_lens.copy_(lens.cpu())
+        assert_attention_close(out, oracle_dense(q_cpu, full), torch.bfloat16, "rank %d eager %d" % (rank, it))
+        bt, ll = stripe_tables(bt_full, lens, 16, nccl.rank, nccl.world)
+        ref = nccl(q, k, v, bt, ll, max_seq_len=L)
+        assert (ref.float() - out.float()).abs().max().item() <= 1e-2
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for it in range(3):
+        lens.copy_(torch.randint(0, L + 1, (len(lens0),), generator=g, dtype=torch.int32))
+        graph.replay()
+        torch.cuda.synchronize()
+        full.seq_lens.copy_(lens.cpu())
+        assert_attention_close(out, oracle_dense(q_cpu, full), torch.bfloat16, "rank %d graph %d" % (rank, it))
+    del graph
+    assert attn.p2p_errors() == 0
+    dist.barrier()
+    dist.destroy_process_group()
+    print("rank", rank, "ok")
+    """
+)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_peer_memory_exchange():
+    script = _P2P_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
+    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    f = os.path.join(path, "seq_sharded_p2p_case.py")
+    with open(f, "w") as fh:
+        fh.write(script)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29539", f],
+                       capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("ok") == 2
