@@ -96,17 +96,23 @@ constexpr int tma_stages() {
   return TmaShape<D>::kStages;
 }
 
-// e4m3 caches: half the bytes per tile, so a deeper ring keeps as many bytes
-// in flight per CTA.
+// e4m3 caches: each consumer warp takes two 16-token slices per tile (their
+// math is the limit, not HBM), so a tile holds as many bytes as a 16-bit one.
 #ifndef DK_TMA_FP8_STAGES
-#define DK_TMA_FP8_STAGES 4
+#define DK_TMA_FP8_STAGES 2
+#endif
+#ifndef DK_TMA_FP8_SLICES
+#define DK_TMA_FP8_SLICES 2
 #endif
 template <int D>
 struct TmaShapeFp8 {
   static constexpr int kStages = DK_TMA_FP8_STAGES;
   static constexpr int kWarps = TmaShape<D>::kWarps;
-  using Cfg = TmaConfig<D, kStages, kWarps, 1>;
+  static constexpr int kSlices = DK_TMA_FP8_SLICES;
+  using Cfg = TmaConfig<D, kStages, kWarps, 1, kSlices>;
 };
+
+int tma_tile_fp8(int D) { return D == 128 ? TmaShapeFp8<128>::Cfg::kTile : TmaShapeFp8<256>::Cfg::kTile; }
 
 int tma_tile(int D) {
   return D == 64 ? TmaShape<64>::Cfg::kTile : (D == 128 ? TmaShape<128>::Cfg::kTile : TmaShape<256>::Cfg::kTile);
@@ -308,6 +314,8 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
     ps = a.partition_size > 0 ? a.partition_size
                               : desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L, num_sms(dev),
                                                        a.kv_fp8 ? 1 : 2);
+    if (a.partition_size == 0 && a.kv_fp8 && pl->path == DK_PATH_TMA_MMA && a.head_dim >= 128)
+      ps = round_up(ps, tma_tile_fp8(a.head_dim));  // whole e4m3 tiles
     parts = ceil_div(L, ps);
     if (parts > a.max_partitions) {  // the caller's workspace caps the partition count
       ps = round_up(ceil_div(L, a.max_partitions), DK_TILE_TOKENS);
@@ -500,7 +508,8 @@ int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
     if constexpr (D >= 128) {
       using Shape = TmaShapeFp8<D>;
       static bool attr_done[kMaxDevices] = {false};
-      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true>, Shape::Cfg::kThreads,
+      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices>,
+                          Shape::Cfg::kThreads,
                           Shape::Cfg::kSmemBytes, dev, attr_done);
     }
     return 0;
@@ -542,7 +551,7 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
     if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
       using Shape = TmaShapeFp8<D>;
       static bool attr_done[kMaxDevices] = {false};
-      auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true>;
+      auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices>;
       const int smem = Shape::Cfg::kSmemBytes;
       e = ensure_smem_attr(kernel, smem, dev, attr_done);
       if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(fp8 partition kernel)");
@@ -613,7 +622,8 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.block_size = a.block_size;
   p.num_blocks = a.num_blocks;
   p.bs_log2 = ilog2(a.block_size);
-  p.rows_log2 = std::min(p.bs_log2, ilog2(tma_tile(a.head_dim)));
+  p.rows_log2 = std::min(p.bs_log2, ilog2(pl.path == DK_PATH_TMA_MMA && a.kv_fp8 ? tma_tile_fp8(a.head_dim)
+                                                                               : tma_tile(a.head_dim)));
   p.partition_size = pl.partition_size;
   p.num_partitions = pl.num_partitions;
   p.ws_partitions = pl.split ? a.max_partitions : 1;

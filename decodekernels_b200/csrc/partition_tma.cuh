@@ -39,16 +39,20 @@ namespace dkb {
 // (64 for head_dim <= 128, 32 for head_dim 256 so that several CTAs fit on
 // an SM); a tile divides the 64-token partition granularity.  KV_BYTES is the
 // cache element size (2, or 1 for e4m3 caches).
-template <int D, int NSTAGES, int WARPS, int KV_BYTES = 2>
+template <int D, int NSTAGES, int WARPS, int KV_BYTES = 2, int SLICES = 1>
 struct TmaConfig {
   static constexpr int kWarps = WARPS;
-  static constexpr int kTile = kSubTokens * WARPS;                 // tokens per pipeline stage
+  static constexpr int kTile = kSubTokens * WARPS * SLICES;        // tokens per pipeline stage
   static constexpr int kThreads = (WARPS + 1) * 32;                // + one TMA producer warp
   static constexpr int kHalves = D * KV_BYTES / 128;               // 128-byte column blocks per row
   static constexpr int kTileBytes = kHalves * kTile * 128;         // K (or V) of one tile
   static constexpr int kStageBytes = 2 * kTileBytes;               // K + V
   static constexpr int kSmemBytes = NSTAGES * kStageBytes + 1024;  // + alignment slack
-  static_assert(kTileTokens % kTile == 0, "a tile must divide the partition granularity");
+  // a tile of 64 tokens or fewer divides the partition granularity; larger
+  // ones rely on the planner's partitions being whole tiles (the kernel masks
+  // the rest of a partial tile either way)
+  static_assert(kTileTokens % kTile == 0 || kTile % kTileTokens == 0, "tile and partition granularity");
+  static_assert(kTile / 8 <= 16, "a tile spans at most 16 pages (two producer lanes each)");
   static_assert(RedLayout<D>::floats(WARPS) * 4 <= NSTAGES * kStageBytes, "merge scratch must fit");
 };
 
@@ -57,12 +61,14 @@ struct TmaConfig {
 // blocks [h][row][128 B] followed by the V column blocks.
 //
 // FP8: the caches hold e4m3 bytes (rows of D bytes, D / 128 column blocks);
-// the consumers convert in registers (tile_math_fp8.cuh).
-template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false>
+// the consumers convert in registers (tile_math_fp8.cuh).  SLICES: 16-token
+// slices per consumer warp and tile (2: the warp's two slices share one
+// softmax update, for the e4m3 path whose consumers bound the throughput).
+template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false, int SLICES = 1>
 __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap k_map,
                                                                        const __grid_constant__ CUtensorMap v_map,
                                                                        const DecodeParams p) {
-  using Cfg = TmaConfig<D, NSTAGES, WARPS, FP8 ? 1 : 2>;
+  using Cfg = TmaConfig<D, NSTAGES, WARPS, FP8 ? 1 : 2, SLICES>;
   constexpr int TILE = Cfg::kTile;
   constexpr int H = Cfg::kHalves;
 
@@ -98,14 +104,16 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   // Inputs written by the previous kernel in the stream are visible after this.
   pdl_wait_primary();
 
-  // Producer lane k (k < 8) addresses page k of each tile and issues its box;
-  // lanes 8-15 issue the V boxes of separate K/V caches.  The block ids of the
-  // first tile are fetched together with the length (entries below
-  // max_seq_len are inside the block-table row), later ones one tile ahead.
+  // Producer lane k (k < PAGES, the most pages a tile spans) addresses page k
+  // of each tile and issues its box; lanes PAGES..2*PAGES-1 issue the V boxes
+  // of separate K/V caches.  The block ids of the first tile are fetched
+  // together with the length (entries below max_seq_len are inside the
+  // block-table row), later ones one tile ahead.
+  constexpr int PAGES = TILE / 8;  // block size >= 8 on this path
   const int pstart = part * p.partition_size;
-  const int kslot = lane & 7;
-  const bool v_lane = lane >= 8 && lane < 16 && !p.kv_fused;
-  const bool box_lane = warp == WARPS && (lane < 8 || v_lane);
+  const int kslot = lane % PAGES;
+  const bool v_lane = lane >= PAGES && lane < 2 * PAGES && !p.kv_fused;
+  const bool box_lane = warp == WARPS && (lane < PAGES || v_lane);
   const int bs_log2 = p.bs_log2;
   const int bs_mask = (1 << bs_log2) - 1;
   const int* bt = p.block_tables + static_cast<int64_t>(seq) * p.bt_stride;
@@ -170,7 +178,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   float scale_log2 = p.scale_log2;
   if constexpr (FP8) scale_log2 *= wa.q_scale;
   const StageGeom<H> geom(rows_log2);
-  const int r0 = warp * kSubTokens;  // first tile row of this warp
+  const int r0 = warp * kSubTokens * SLICES;  // first tile row of this warp
   const uint32_t smem_base = smem_u32(smem);
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % NSTAGES;
@@ -178,7 +186,10 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
     const int sub0 = pstart + t * TILE + r0;  // first token of this warp's 16
     if (sub0 < pend) {
       if (!mbar_wait(&full_bar[s], parity)) break;
-      wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
+      if constexpr (SLICES == 2)
+        wa.slice2(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
+      else
+        wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);

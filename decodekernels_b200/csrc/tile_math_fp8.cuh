@@ -185,6 +185,133 @@ struct WarpAttentionFp8 {
     }
   }
 
+  // K chunk pair kk, kk + 1 of one 16-row slice -> A fragments (permuted columns).
+  __device__ __forceinline__ static void k_frags(uint32_t addr, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+    uint32_t r[4];
+    ldmatrix_x4(r, addr);
+    a0[0] = e4m3x2_to_f16x2(r[0] & 0xFFFFu);
+    a0[1] = e4m3x2_to_f16x2(r[1] & 0xFFFFu);
+    a0[2] = e4m3x2_to_f16x2(r[0] >> 16);
+    a0[3] = e4m3x2_to_f16x2(r[1] >> 16);
+    a1[0] = e4m3x2_to_f16x2(r[2] & 0xFFFFu);
+    a1[1] = e4m3x2_to_f16x2(r[3] & 0xFFFFu);
+    a1[2] = e4m3x2_to_f16x2(r[2] >> 16);
+    a1[3] = e4m3x2_to_f16x2(r[3] >> 16);
+  }
+
+  // V chunk pair mt, mt + 1 of one 16-row slice -> row-permuted V^T A fragments.
+  __device__ __forceinline__ static void v_frags(uint32_t addr, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+    uint32_t r[4];
+    ldmatrix_x4_trans(r, addr);
+    uint32_t x0 = prmt(r[0], 0u, 0x3120u);
+    uint32_t x1 = prmt(r[1], 0u, 0x3120u);
+    a0[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
+    a0[1] = e4m3x2_to_f16x2(x0 >> 16);
+    a0[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
+    a0[3] = e4m3x2_to_f16x2(x1 >> 16);
+    x0 = prmt(r[2], 0u, 0x3120u);
+    x1 = prmt(r[3], 0u, 0x3120u);
+    a1[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
+    a1[1] = e4m3x2_to_f16x2(x0 >> 16);
+    a1[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
+    a1[3] = e4m3x2_to_f16x2(x1 >> 16);
+  }
+
+  // Two 16-token slices (tile rows r0..r0+31, first token sub0) with one
+  // softmax update: their K chains and conversions interleave, and the
+  // running max, the rescale and the exp-sum update happen once per 32
+  // tokens instead of once per 16.
+  __device__ __forceinline__ void slice2(uint32_t sb, const StageGeom<H>& g, int r0, int sub0, int pend,
+                                         float scale_log2, int lane) {
+    const int ra = r0 + (lane & 7) + (((lane >> 3) & 1) << 3);  // slice A row of this lane's ldmatrix address
+    const int rb = ra + kSubTokens;                              // slice B
+    const int half = lane >> 4;
+    const uint32_t ka = sb + g.k_row(ra), kb = sb + g.k_row(rb);
+    const uint32_t va = sb + g.v_row(ra), vb = sb + g.v_row(rb);
+    const int swa = ra & 7, swb = rb & 7;
+
+    float sA0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sA1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float sB0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, sB1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int kk = 0; kk < MT; kk += 2) {
+      const int chunk = kk + half;
+      uint32_t aA0[4], aA1[4], aB0[4], aB1[4];
+      k_frags(ka + (chunk >> 3) * g.hstride + (((chunk & 7) ^ swa) << 4), aA0, aA1);
+      k_frags(kb + (chunk >> 3) * g.hstride + (((chunk & 7) ^ swb) << 4), aB0, aB1);
+      Mma<__half>::run(sA0, aA0, qf[kk][0], qf[kk][1]);
+      Mma<__half>::run(sB0, aB0, qf[kk][0], qf[kk][1]);
+      Mma<__half>::run(sA1, aA1, qf[kk + 1][0], qf[kk + 1][1]);
+      Mma<__half>::run(sB1, aB1, qf[kk + 1][0], qf[kk + 1][1]);
+    }
+    float sa[4], sbb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      sa[i] = (sA0[i] + sA1[i]) * scale_log2;
+      sbb[i] = (sB0[i] + sB1[i]) * scale_log2;
+    }
+    const int tok = sub0 + (lane >> 2);
+    if (tok >= pend) sa[0] = sa[1] = -INFINITY;
+    if (tok + 8 >= pend) sa[2] = sa[3] = -INFINITY;
+    if (tok + 16 >= pend) sbb[0] = sbb[1] = -INFINITY;
+    if (tok + 24 >= pend) sbb[2] = sbb[3] = -INFINITY;
+
+    float mx0 = fmaxf(fmaxf(sa[0], sa[2]), fmaxf(sbb[0], sbb[2]));
+    float mx1 = fmaxf(fmaxf(sa[1], sa[3]), fmaxf(sbb[1], sbb[3]));
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float mn0 = fmaxf(m0, mx0);
+    const float mn1 = fmaxf(m1, mx1);
+    const float al0 = fast_exp2(m0 - mn0);
+    const float al1 = fast_exp2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    const float pa0 = fast_exp2(sa[0] - mn0), pa1 = fast_exp2(sa[1] - mn1);
+    const float pa2 = fast_exp2(sa[2] - mn0), pa3 = fast_exp2(sa[3] - mn1);
+    const float pb0 = fast_exp2(sbb[0] - mn0), pb1 = fast_exp2(sbb[1] - mn1);
+    const float pb2 = fast_exp2(sbb[2] - mn0), pb3 = fast_exp2(sbb[3] - mn1);
+    l0 = fmaf(l0, al0, (pa0 + pa2) + (pb0 + pb2));
+    l1 = fmaf(l1, al1, (pa1 + pa3) + (pb1 + pb3));
+    if (__any_sync(0xffffffffu, al0 != 1.0f || al1 != 1.0f)) {  // skipped once the running maxima settle
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        acc[mt][0] *= al0;
+        acc[mt][1] *= al1;
+        acc[mt][2] *= al0;
+        acc[mt][3] *= al1;
+      }
+    }
+    const uint32_t PA0 = movmatrix_trans(Conv<__half>::pack2(pa0, pa1));
+    const uint32_t PA1 = movmatrix_trans(Conv<__half>::pack2(pa2, pa3));
+    const uint32_t PB0 = movmatrix_trans(Conv<__half>::pack2(pb0, pb1));
+    const uint32_t PB1 = movmatrix_trans(Conv<__half>::pack2(pb2, pb3));
+
+    if (sub0 + 2 * kSubTokens > pend) {
+      // rows of tokens >= pend hold stale bytes (possibly NaN codes): clear them
+      const int first_bad = r0 + max(pend - sub0, 0);
+      for (int i = lane; i < 2 * kSubTokens * H * 8; i += 32) {
+        const int rr = r0 + i / (H * 8);
+        const int rem = i % (H * 8);
+        if (rr >= first_bad) st_shared_zero16(sb + g.v_row(rr) + (rem >> 3) * g.hstride + ((rem & 7) << 4));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; mt += 2) {
+      const int chunk = mt + half;
+      uint32_t aA0[4], aA1[4], aB0[4], aB1[4];
+      v_frags(va + (chunk >> 3) * g.hstride + (((chunk & 7) ^ swa) << 4), aA0, aA1);
+      v_frags(vb + (chunk >> 3) * g.hstride + (((chunk & 7) ^ swb) << 4), aB0, aB1);
+      Mma<__half>::run(acc[mt], aA0, PA0, PA1);
+      Mma<__half>::run(acc[mt + 1], aA1, PA0, PA1);
+      Mma<__half>::run(acc[mt], aB0, PB0, PB1);
+      Mma<__half>::run(acc[mt + 1], aB1, PB0, PB1);
+    }
+  }
+
   // Finish the exp-sums and store this warp's state into the merge scratch
   // (accumulator row m of block mt is column d = 16 mt + 2 (m % 8) + m / 8).
   __device__ __forceinline__ void to_red(float* red, int warps, int warp, int group, int lane) {

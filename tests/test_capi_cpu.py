@@ -185,7 +185,7 @@ def test_fp8_caches_plan_and_validate():
     a = capi.make_args(q, kv8, kv8, bt, sl, 128**-0.5, 3000, q, _ws(4, 32, 47), 0, False, 0, 0.5, 0.25)
     assert a.kv_fp8 == 1 and a.k_scale == 0.5
     rc, p = _plan(a)
-    assert rc == 0 and p["path"] == capi.DK_PATH_TMA_MMA and p["stages"] == 4
+    assert rc == 0 and p["path"] == capi.DK_PATH_TMA_MMA and p["stages"] == 2 and p["partition_size"] % 128 == 0
     # e4m3 rows of 64 bytes go to the CUDA-core path
     kv64 = torch.zeros(64, 16, 8, 64, dtype=torch.uint8)
     q64 = torch.zeros(4, 32, 64, dtype=torch.bfloat16)
