@@ -14,11 +14,17 @@ backend):
   for an older interleaved layout (``decode_kernels/vllm_patch.py:122``).
   vLLM writes the new token's K/V before ``forward`` runs, so ``seq_lens``
   already includes it.
+* FP8 KV caches (``kv_cache_dtype`` "fp8" / "fp8_e4m3": uint8 e4m3 codes
+  written with the layer's per-tensor scales) decode here too, with
+  ``layer._k_scale_float`` / ``layer._v_scale_float``, as long as the query
+  stays 16-bit.  The reference refuses every quantized cache
+  (``decode_kernels/vllm_patch.py:74``); this library has an e4m3 path.
 * Everything else falls back to the original FlashAttention path through a
   strict eligibility check (``_attention_eligible``): prefill and mixed
-  batches, quantized KV caches, sliding windows, ALiBi, soft-capping, sinks,
-  cascade attention, context parallelism, CUDA-graph capture, head sizes
-  other than 64/128/256 and GQA groups above 8.
+  batches, e5m2 or other quantized caches, fp8 queries, sliding windows,
+  ALiBi, soft-capping, sinks, cascade attention, context parallelism,
+  CUDA-graph capture, head sizes other than 64/128/256 and GQA groups
+  above 8.
 * ``rms_norm`` and ``silu_and_mul`` (the reference's other two patches) are
   not part of this library; asking for them logs a note and changes nothing.
 """
@@ -49,7 +55,23 @@ def reset_stats() -> None:
         _STATS[k] = 0
 
 
-def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_scale, output_block_scale) -> bool:
+_FP8_E4M3 = ("fp8", "fp8_e4m3")
+
+
+def _fp8_scales(layer) -> tuple[float, float] | None:
+    """The layer's per-tensor K/V scales as floats, or None when unusable."""
+    ks, vs = getattr(layer, "_k_scale_float", None), getattr(layer, "_v_scale_float", None)
+    try:
+        ks, vs = float(ks), float(vs)
+    except (TypeError, ValueError):
+        return None
+    if not (0.0 < ks < float("inf") and 0.0 < vs < float("inf")):
+        return None
+    return ks, vs
+
+
+def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_scale, output_block_scale,
+                        layer=None) -> bool:
     """True when this decode batch can run on decodekernels_b200 unchanged."""
     if attn_metadata is None or output_scale is not None or output_block_scale is not None:
         return False
@@ -69,9 +91,16 @@ def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_sca
         return False
     if getattr(impl, "dcp_world_size", 1) > 1:
         return False
-    if str(getattr(impl, "kv_cache_dtype", "auto")) not in ("auto", "float16", "bfloat16"):
+    kv_dtype = str(getattr(impl, "kv_cache_dtype", "auto"))
+    if query.dtype not in _HALF_TYPES:
         return False
-    if query.dtype not in _HALF_TYPES or kv_cache.dtype != query.dtype:
+    if kv_dtype in ("auto", "float16", "bfloat16"):
+        if kv_cache.dtype != query.dtype:
+            return False
+    elif kv_dtype in _FP8_E4M3:
+        if kv_cache.dtype not in (torch.uint8, torch.float8_e4m3fn) or _fp8_scales(layer) is None:
+            return False
+    else:
         return False
     if kv_cache.dim() != 5 or kv_cache.shape[0] != 2:
         return False
@@ -95,13 +124,17 @@ def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_sca
     return True
 
 
-def _decode(impl, query, kv_cache, attn_metadata, output) -> torch.Tensor:
+def _decode(impl, query, kv_cache, attn_metadata, output, layer=None) -> torch.Tensor:
     n = attn_metadata.num_actual_tokens
     key_cache, value_cache = kv_cache.unbind(0)  # two [blocks, bs, heads, D] views, read in place
     q = query[:n].reshape(n, impl.num_heads, impl.head_size)
     out = output[:n].view(n, impl.num_heads, impl.head_size)
+    k_scale, v_scale = 1.0, 1.0
+    if str(getattr(impl, "kv_cache_dtype", "auto")) in _FP8_E4M3:
+        k_scale, v_scale = _fp8_scales(layer)
     dk_ops.paged_attention_decode(q, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
-                                  scale=impl.scale, max_seq_len=attn_metadata.max_seq_len, out=out)
+                                  scale=impl.scale, max_seq_len=attn_metadata.max_seq_len, out=out, k_scale=k_scale,
+                                  v_scale=v_scale)
     return output
 
 
@@ -112,9 +145,9 @@ def _patch_attention() -> None:
 
     def forward(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale=None,
                 output_block_scale=None):
-        if _attention_eligible(self, query, kv_cache, attn_metadata, output, output_scale, output_block_scale):
+        if _attention_eligible(self, query, kv_cache, attn_metadata, output, output_scale, output_block_scale, layer):
             _STATS["attention_kernel_calls"] += 1
-            return _decode(self, query, kv_cache, attn_metadata, output)
+            return _decode(self, query, kv_cache, attn_metadata, output, layer)
         _STATS["attention_fallback_calls"] += 1
         return original(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale,
                         output_block_scale)

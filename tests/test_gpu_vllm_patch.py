@@ -60,3 +60,54 @@ def test_patched_forward_decodes_on_vllm_cache(stride_order, dtype):
     k_cache, v_cache = kv_cache.unbind(0)
     ref = oracle_dense(query, PagedKV(k_cache, v_cache, meta.block_table, meta.seq_lens, bs))
     assert_attention_close(output.view(n, hq, d), ref, dtype, f"vllm {stride_order}")
+
+
+@pytest.mark.parametrize("stride_order", ["nhd", "hnd"])
+def test_patched_forward_decodes_fp8_vllm_cache(stride_order):
+    """vLLM's fp8 (e4m3) cache -- uint8 codes written as x / scale -- with the
+    layer's per-tensor scales decodes here and matches the oracle on the
+    dequantised cache."""
+    from vllm.v1.attention.backend import AttentionType
+    from vllm.v1.attention.backends.flash_attn import FlashAttentionImpl
+
+    from decodekernels_b200 import vllm_patch
+    from gpu_helpers import oracle_dense_fp8
+
+    vllm_patch.apply(["attention"])
+    vllm_patch.reset_stats()
+    dtype, n, hq, hkv, d, bs = torch.bfloat16, 4, 16, 2, 128, 16
+    ks, vs = 0.02, 0.03
+    lens = [5, 900, 2049, 64]
+    nb = sum(-(-L // bs) for L in lens) + 4
+    g = torch.Generator(device="cuda").manual_seed(9)
+    if stride_order == "nhd":
+        vals = torch.randn(2, nb, bs, hkv, d, generator=g, device="cuda")
+        kv_cache = torch.empty(2, nb, bs, hkv, d, dtype=torch.uint8, device="cuda")
+    else:
+        vals = torch.randn(2, nb, hkv, bs, d, generator=g, device="cuda").transpose(2, 3)
+        kv_cache = torch.empty(2, nb, hkv, bs, d, dtype=torch.uint8, device="cuda").transpose(2, 3)
+    kv_cache[0].copy_((vals[0] / ks).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8))
+    kv_cache[1].copy_((vals[1] / vs).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8))
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(10)).to(torch.int32)
+    table = torch.zeros(n, max(-(-L // bs) for L in lens), dtype=torch.int32)
+    off = 0
+    for i, L in enumerate(lens):
+        k = -(-L // bs)
+        table[i, :k] = perm[off:off + k]
+        off += k
+    impl = SimpleNamespace(attn_type=AttentionType.DECODER, dcp_world_size=1, kv_cache_dtype="fp8",
+                           alibi_slopes=None, logits_soft_cap=None, sliding_window=None, sinks=None, head_size=d,
+                           num_heads=hq, num_kv_heads=hkv, scale=d**-0.5)
+    layer = SimpleNamespace(_k_scale_float=ks, _v_scale_float=vs)
+    meta = SimpleNamespace(max_query_len=1, use_cascade=False, causal=True, num_actual_tokens=n,
+                           seq_lens=torch.tensor(lens, dtype=torch.int32, device="cuda"), block_table=table.cuda(),
+                           max_seq_len=max(lens))
+    query = torch.randn(n, hq, d, generator=g, device="cuda", dtype=dtype)
+    output = torch.full((n, hq * d), float("nan"), device="cuda", dtype=dtype)
+    ret = FlashAttentionImpl.forward(impl, layer, query, None, None, kv_cache, meta, output)
+    torch.cuda.synchronize()
+    assert ret is output and vllm_patch.stats()["attention_kernel_calls"] == 1
+    k8, v8 = kv_cache.unbind(0)
+    kv = PagedKV(k8, v8, meta.block_table, meta.seq_lens, bs)
+    assert_attention_close(output.view(n, hq, d), oracle_dense_fp8(query, kv, k8, v8, ks, vs), dtype,
+                           f"vllm fp8 {stride_order}")

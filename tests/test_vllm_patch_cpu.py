@@ -50,7 +50,8 @@ def test_pure_decode_is_eligible():
     {"attn_metadata": None},                             # profiling run
     {"attn_metadata.use_cascade": True},
     {"impl.dcp_world_size": 2},                          # decode context parallelism
-    {"impl.kv_cache_dtype": "fp8"},
+    {"impl.kv_cache_dtype": "fp8"},                     # fp8 needs a uint8 cache and the layer's scales
+    {"impl.kv_cache_dtype": "fp8_e5m2", "kv_cache": torch.zeros(2, 10, 16, 2, 128, dtype=torch.uint8)},
     {"impl.alibi_slopes": torch.ones(8)},
     {"impl.logits_soft_cap": 30.0},
     {"impl.sliding_window": (127, 0)},
@@ -64,6 +65,22 @@ def test_pure_decode_is_eligible():
 ])
 def test_refusals_fall_back(over):
     assert not vllm_patch._attention_eligible(**_case(**over))
+
+
+def test_fp8_e4m3_cache_with_layer_scales_is_eligible():
+    layer = SimpleNamespace(_k_scale_float=0.02, _v_scale_float=0.5)
+    fp8 = torch.zeros(2, 10, 16, 2, 128, dtype=torch.uint8)
+    for kvd in ("fp8", "fp8_e4m3"):
+        assert vllm_patch._attention_eligible(**_case(**{"impl.kv_cache_dtype": kvd, "kv_cache": fp8}), layer=layer)
+        assert vllm_patch._attention_eligible(
+            **_case(**{"impl.kv_cache_dtype": kvd, "kv_cache": fp8.view(torch.float8_e4m3fn)}), layer=layer)
+    # no layer / unusable scales / an fp8 query fall back
+    assert not vllm_patch._attention_eligible(**_case(**{"impl.kv_cache_dtype": "fp8", "kv_cache": fp8}))
+    bad = SimpleNamespace(_k_scale_float=0.0, _v_scale_float=1.0)
+    assert not vllm_patch._attention_eligible(**_case(**{"impl.kv_cache_dtype": "fp8", "kv_cache": fp8}), layer=bad)
+    q8 = torch.zeros(3, 8, 128, dtype=torch.float8_e4m3fn)
+    assert not vllm_patch._attention_eligible(**_case(**{"impl.kv_cache_dtype": "fp8", "kv_cache": fp8,
+                                                         "query": q8}), layer=layer)
 
 
 def test_non_contiguous_output_falls_back():
