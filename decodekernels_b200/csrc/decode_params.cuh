@@ -32,6 +32,7 @@ struct DecodeParams {
   int64_t k_stride_block, k_stride_token, k_stride_head;
   int64_t v_stride_block, v_stride_token, v_stride_head;
   int64_t bt_stride;
+  int num_seqs;
   int num_q_heads;
   int num_kv_heads;
   int group;           // num_q_heads / num_kv_heads
@@ -50,5 +51,20 @@ struct DecodeParams {
   float v_scale;       // e4m3 caches: V = code * v_scale (1 otherwise), applied to the partition results
   int kv_fp8;          // 1: the caches hold e4m3 bytes
 };
+
+// (partition, kv_head, seq) of this CTA in the 1-D grid, sequence-major:
+// a (seq, kv_head)'s partitions are consecutive, so a long sequence's work is
+// spread over the whole grid.  (Partition-major order, which pushes the
+// early-exit CTAs past short sequences' ends to the back, measured 10% slower
+// on skewed lengths -- it also pushes long sequences' last partitions into
+// the tail -- and within 2% elsewhere.)
+__device__ __forceinline__ void cta_coords(int num_partitions, int num_kv_heads, int& part, int& kv_head, int& seq) {
+  const unsigned b = blockIdx.x;
+  const unsigned np = static_cast<unsigned>(num_partitions);
+  const unsigned pair = b / np;
+  part = static_cast<int>(b - pair * np);
+  seq = static_cast<int>(pair / static_cast<unsigned>(num_kv_heads));
+  kv_head = static_cast<int>(pair - static_cast<unsigned>(seq) * static_cast<unsigned>(num_kv_heads));
+}
 
 }  // namespace dkb

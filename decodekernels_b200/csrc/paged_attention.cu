@@ -544,8 +544,7 @@ int plan_occupancy(const DkPagedAttnArgs& a, const DkPlan& pl, int dev) {
 
 template <typename T, int D>
 int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
-  const dim3 grid(static_cast<unsigned>(pl.num_partitions), static_cast<unsigned>(a.num_kv_heads),
-                  static_cast<unsigned>(a.num_seqs));
+  const dim3 grid(static_cast<unsigned>(pl.num_ctas));  // 1-D, sequence-major (cta_coords)
   cudaError_t e;
   if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
     if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
@@ -591,6 +590,9 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
 }
 
 int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream, bool lse_mode = false) {
+  if (1LL * pl.num_partitions * a.num_kv_heads * a.num_seqs > INT_MAX)
+    return fail(1, "paged_attention_decode: %d partitions x %d KV heads x %d sequences exceed one grid", pl.num_partitions,
+                a.num_kv_heads, a.num_seqs);
   DecodeParams p;
   std::memset(&p, 0, sizeof(p));
   p.lse_mode = lse_mode ? 1 : 0;
@@ -615,6 +617,7 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.v_stride_token = a.v_stride_token;
   p.v_stride_head = a.v_stride_head;
   p.bt_stride = a.bt_stride;
+  p.num_seqs = a.num_seqs;
   p.num_q_heads = a.num_q_heads;
   p.num_kv_heads = a.num_kv_heads;
   p.group = a.num_q_heads / a.num_kv_heads;

@@ -43,9 +43,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
   using Vec = VecT<KV, V>;
   extern __shared__ float simt_smem[];
 
-  const int part = blockIdx.x;
-  const int kv_head = blockIdx.y;
-  const int seq = blockIdx.z;
+  int part, kv_head, seq;
+  cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int group = p.group;

@@ -77,9 +77,8 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   __shared__ __align__(8) uint64_t full_bar[NSTAGES];
   __shared__ __align__(8) uint64_t empty_bar[NSTAGES];
 
-  const int part = blockIdx.x;
-  const int kv_head = blockIdx.y;
-  const int seq = blockIdx.z;
+  int part, kv_head, seq;
+  cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rows_log2 = p.rows_log2;
