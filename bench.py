@@ -441,8 +441,12 @@ def run_gpu_arm(args) -> None:
     ee.record(stream)
     torch.cuda.synchronize()
     e2e_s = es.elapsed_time(ee) * 1e-3
-    if not torch.equal(h_outs[(e_steps - 1) % 2], out.cpu()):
-        raise SystemExit(f"rank {rank}: the end-to-end output differs from the device-timed call's")
+    e2e_out, dev_out = h_outs[(e_steps - 1) % 2].float(), out.float().cpu()
+    if not torch.equal(e2e_out, dev_out):
+        diff = (e2e_out - dev_out).abs()
+        raise SystemExit(f"rank {rank}: the end-to-end output differs from the device-timed call's: "
+                         f"{int((diff > 0).sum())} elements, max {float(diff.nan_to_num(0.0).max()):.3e}, "
+                         f"NaN {int(torch.isnan(e2e_out).sum())} / {int(torch.isnan(dev_out).sum())}")
     if flush:  # remove the flush time from the end-to-end window
         fs, fe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         fs.record(stream)

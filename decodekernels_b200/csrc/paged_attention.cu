@@ -314,14 +314,15 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
     ps = round_up(L, DK_TILE_TOKENS);  // no workspace: one pass over the whole sequence
     parts = 1;
   } else {
+    // granularity of a chosen size: whole tiles of the kernel that runs
+    const int gran = a.kv_fp8 && pl->path == DK_PATH_TMA_MMA ? tma_tile_fp8(a.head_dim) : DK_TILE_TOKENS;
     ps = a.partition_size > 0 ? a.partition_size
-                              : desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L, num_sms(dev),
-                                                       a.kv_fp8 ? 1 : 2);
-    if (a.partition_size == 0 && a.kv_fp8 && pl->path == DK_PATH_TMA_MMA && a.head_dim >= 128)
-      ps = round_up(ps, tma_tile_fp8(a.head_dim));  // whole e4m3 tiles
+                              : round_up(desired_partition_size(a.num_seqs, a.num_kv_heads, a.head_dim, L,
+                                                                num_sms(dev), a.kv_fp8 ? 1 : 2),
+                                         gran);
     parts = ceil_div(L, ps);
     if (parts > a.max_partitions) {  // the caller's workspace caps the partition count
-      ps = round_up(ceil_div(L, a.max_partitions), DK_TILE_TOKENS);
+      ps = round_up(ceil_div(L, a.max_partitions), gran);
       parts = ceil_div(L, ps);
     }
   }

@@ -183,13 +183,17 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
     const int s = t % NSTAGES;
     const uint32_t parity = (t / NSTAGES) & 1;
     const int sub0 = pstart + t * TILE + r0;  // first token of this warp's 16
-    if (sub0 < pend) {
-      if (!mbar_wait(&full_bar[s], parity)) break;
-      if constexpr (SLICES == 2)
-        wa.slice2(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
-      else
-        wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
-    }
+    // Only the last tile can start past this warp's rows.  Such a warp must
+    // not arrive on that stage's empty barrier: with no full-barrier wait to
+    // hold it back, its arrival could count towards the pending phase of the
+    // tile NSTAGES earlier while a slower warp still reads that tile, and the
+    // producer would overwrite it.  No one waits for the last tile's phase.
+    if (sub0 >= pend) break;
+    if (!mbar_wait(&full_bar[s], parity)) break;
+    if constexpr (SLICES == 2)
+      wa.slice2(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
+    else
+      wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[s]);
   }
