@@ -24,6 +24,7 @@ DK_DTYPE_FP8_E4M3 = 2
 DK_PATH_NONE, DK_PATH_TMA_MMA, DK_PATH_SIMT = 0, 1, 2
 DK_FLAG_FORCE_SIMT = 1
 DK_FLAG_FORCE_FUSED_MERGE = 2
+DK_FLAG_PERSISTENT = 4
 DK_MAX_GQA_GROUP = 8
 DK_TILE_TOKENS = 64
 DK_REF_PARTITION_SIZE = 512

@@ -50,6 +50,8 @@ struct DecodeParams {
   float scale_log2;    // softmax scale * log2(e) (* k_scale for e4m3 caches)
   float v_scale;       // e4m3 caches: V = code * v_scale (1 otherwise), applied to the partition results
   int kv_fp8;          // 1: the caches hold e4m3 bytes
+  int compact;         // 1: live work items numbered densely (compact_coords); CTA b runs items b, b + G, ...
+  int persistent;      // 1 (with compact): the grid is one wave of resident CTAs
 };
 
 // (partition, kv_head, seq) of this CTA in the 1-D grid, sequence-major:
@@ -65,6 +67,75 @@ __device__ __forceinline__ void cta_coords(int num_partitions, int num_kv_heads,
   part = static_cast<int>(b - pair * np);
   seq = static_cast<int>(pair / static_cast<unsigned>(num_kv_heads));
   kv_head = static_cast<int>(pair - static_cast<unsigned>(seq) * static_cast<unsigned>(num_kv_heads));
+}
+
+// Compact grid: the live work items -- every (seq, kv_head, partition) with
+// partition < max(1, ceil(L / partition_size)), L = min(seq_lens[seq],
+// max_seq_len), in sequence-major order as above -- numbered densely; CTA b
+// of a grid of G runs items b, b + G, ... (G is a few waves of resident
+// CTAs, so it is usually one item).  For lengths far below max_seq_len most
+// CTAs of the dense grid have no tokens, and interleaved with the live ones
+// they slow the hardware's dispatch of the live CTAs (c4 with e4m3 caches:
+// 938 live CTAs of 8192).  An empty sequence keeps its partition-0 item (it
+// may write zeros).
+constexpr int kCompactMaxSeqs = 512;
+constexpr int kCompactPerLane = kCompactMaxSeqs / 32;
+
+// Item `target` of the compact numbering, computed by one warp (all 32 lanes):
+// lane l loads the lengths of sequences [l * per, (l + 1) * per) in one
+// batch, a warp scan of the lanes' item counts finds the owner lane by
+// ballot, and the owner walks its sequences.  Also returns the item's
+// sequence length (clamped to [0, max_seq_len]).  False past the last item.
+__device__ __forceinline__ bool compact_coords(const DecodeParams& p, unsigned target, int lane, int& part,
+                                               int& kv_head, int& seq, int& seq_len) {
+  const int per = (p.num_seqs + 31) >> 5;  // <= kCompactPerLane
+  const int first = lane * per;
+  const unsigned ps = static_cast<unsigned>(p.partition_size);
+  const unsigned hkv = static_cast<unsigned>(p.num_kv_heads);
+  int len[kCompactPerLane];
+#pragma unroll
+  for (int j = 0; j < kCompactPerLane; ++j)
+    len[j] = j < per && first + j < p.num_seqs ? max(min(__ldg(p.seq_lens + first + j), p.max_seq_len), 0) : -1;
+  unsigned parts[kCompactPerLane];
+  unsigned mine = 0;
+#pragma unroll
+  for (int j = 0; j < kCompactPerLane; ++j) {
+    parts[j] = len[j] < 0 ? 0u : 1u;  // an empty sequence keeps one item
+    if (len[j] > static_cast<int>(ps)) parts[j] = (static_cast<unsigned>(len[j]) + ps - 1) / ps;
+    mine += parts[j];
+  }
+  mine *= hkv;
+  unsigned incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (target >= __shfl_sync(0xffffffffu, incl, 31)) return false;
+  const int owner = __ffs(__ballot_sync(0xffffffffu, incl > target)) - 1;
+  int f_seq = 0, f_head = 0, f_part = 0, f_len = 0;
+  if (lane == owner) {
+    unsigned r = target - (incl - mine);
+    bool found = false;
+#pragma unroll
+    for (int j = 0; j < kCompactPerLane; ++j) {
+      const unsigned items = parts[j] * hkv;
+      if (!found && r < items) {
+        found = true;
+        f_seq = first + j;
+        f_head = static_cast<int>(r / parts[j]);
+        f_part = static_cast<int>(r - static_cast<unsigned>(f_head) * parts[j]);
+        f_len = len[j];
+      } else if (!found) {
+        r -= items;
+      }
+    }
+  }
+  seq = __shfl_sync(0xffffffffu, f_seq, owner);
+  kv_head = __shfl_sync(0xffffffffu, f_head, owner);
+  part = __shfl_sync(0xffffffffu, f_part, owner);
+  seq_len = __shfl_sync(0xffffffffu, f_len, owner);
+  return true;
 }
 
 }  // namespace dkb

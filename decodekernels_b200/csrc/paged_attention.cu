@@ -88,6 +88,8 @@ template <int D>
 struct TmaShape {
   static constexpr int kStages = D == 64 ? DK_TMA_STAGES_D64 : (D == 128 ? DK_TMA_STAGES_D128 : DK_TMA_STAGES_D256);
   static constexpr int kWarps = D == 64 ? DK_TMA_WARPS_D64 : (D == 128 ? DK_TMA_WARPS_D128 : DK_TMA_WARPS_D256);
+  static constexpr int kSlices = 1;
+  static constexpr int kMinCtas = 0;
   using Cfg = TmaConfig<D, kStages, kWarps>;
 };
 
@@ -101,14 +103,30 @@ constexpr int tma_stages() {
 #ifndef DK_TMA_FP8_STAGES
 #define DK_TMA_FP8_STAGES 2
 #endif
-#ifndef DK_TMA_FP8_SLICES
-#define DK_TMA_FP8_SLICES 2
+#ifndef DK_TMA_FP8_SLICES_D128
+#define DK_TMA_FP8_SLICES_D128 2
+#endif
+#ifndef DK_TMA_FP8_SLICES_D256
+#define DK_TMA_FP8_SLICES_D256 2
+#endif
+#ifndef DK_TMA_FP8_WARPS_D128
+#define DK_TMA_FP8_WARPS_D128 DK_TMA_WARPS_D128
+#endif
+#ifndef DK_TMA_FP8_WARPS_D256
+#define DK_TMA_FP8_WARPS_D256 DK_TMA_WARPS_D256
+#endif
+#ifndef DK_TMA_FP8_MIN_CTAS_D128
+#define DK_TMA_FP8_MIN_CTAS_D128 0
+#endif
+#ifndef DK_TMA_FP8_MIN_CTAS_D256
+#define DK_TMA_FP8_MIN_CTAS_D256 0
 #endif
 template <int D>
 struct TmaShapeFp8 {
   static constexpr int kStages = DK_TMA_FP8_STAGES;
-  static constexpr int kWarps = TmaShape<D>::kWarps;
-  static constexpr int kSlices = DK_TMA_FP8_SLICES;
+  static constexpr int kWarps = D == 128 ? DK_TMA_FP8_WARPS_D128 : DK_TMA_FP8_WARPS_D256;
+  static constexpr int kSlices = D == 128 ? DK_TMA_FP8_SLICES_D128 : DK_TMA_FP8_SLICES_D256;
+  static constexpr int kMinCtas = D == 128 ? DK_TMA_FP8_MIN_CTAS_D128 : DK_TMA_FP8_MIN_CTAS_D256;
   using Cfg = TmaConfig<D, kStages, kWarps, 1, kSlices>;
 };
 
@@ -243,6 +261,17 @@ int validate(const DkPagedAttnArgs* a) {
 #ifndef DK_FUSED_MERGE_MAX_BYTES
 #define DK_FUSED_MERGE_MAX_BYTES (64 * 1024)
 #endif
+// Compact grid (compact_coords): from this many partitions per sequence,
+// for up to kCompactMaxSeqs sequences (a warp scans them all in every CTA);
+// the grid is this many waves of resident CTAs at most.
+#ifndef DK_COMPACT_MIN_PARTITIONS
+#define DK_COMPACT_MIN_PARTITIONS 16
+#endif
+#ifndef DK_COMPACT_WAVES
+#define DK_COMPACT_WAVES 4
+#endif
+constexpr int kCompactMinPartitions = DK_COMPACT_MIN_PARTITIONS;
+constexpr int kCompactWaves = DK_COMPACT_WAVES;
 constexpr long long kFusedMergeMaxBytes = DK_FUSED_MERGE_MAX_BYTES;
 constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
 constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
@@ -512,7 +541,7 @@ int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
     if constexpr (D >= 128) {
       using Shape = TmaShapeFp8<D>;
       static bool attr_done[kMaxDevices] = {false};
-      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices>,
+      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices, Shape::kMinCtas>,
                           Shape::Cfg::kThreads,
                           Shape::Cfg::kSmemBytes, dev, attr_done);
     }
@@ -546,36 +575,64 @@ int plan_occupancy(const DkPagedAttnArgs& a, const DkPlan& pl, int dev) {
   }
 }
 
+// CTAs of a compact grid (compact_coords): `waves` waves of the kernel's
+// resident CTAs, at most one per work item of the dense grid.  The
+// occupancy is queried once per kernel and device (cache; -1: unknown, which
+// keeps the dense size).
+template <typename Kernel>
+unsigned compact_grid(Kernel kernel, int threads, int smem, int dev, int dense, int waves, int* cache) {
+  if (dev < 0 || dev >= kMaxDevices) return static_cast<unsigned>(dense);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, static_cast<size_t>(smem)) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    cache[dev] = n > 0 ? n : -1;
+  }
+  if (cache[dev] < 0) return static_cast<unsigned>(dense);
+  return static_cast<unsigned>(std::min<long long>(dense, 1LL * waves * cache[dev] * num_sms(dev)));
+}
+
+// One TMA partition kernel instance: e4m3 or 16-bit caches, dense or
+// compact grid.
+template <typename T, int D, bool FP8, bool COMPACT>
+int launch_tma(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
+  using Shape = std::conditional_t<FP8, TmaShapeFp8<D>, TmaShape<D>>;
+  static bool attr_done[kMaxDevices] = {false};
+  static int occ[kMaxDevices] = {0};
+  auto kernel =
+      paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, FP8, Shape::kSlices, Shape::kMinCtas, COMPACT>;
+  const int smem = Shape::Cfg::kSmemBytes;
+  cudaError_t e = ensure_smem_attr(kernel, smem, dev, attr_done);
+  if (e != cudaSuccess)
+    return fail_cuda(e, FP8 ? "cudaFuncSetAttribute(fp8 partition kernel)" : "cudaFuncSetAttribute(partition kernel)");
+  dim3 grid(static_cast<unsigned>(pl.num_ctas));
+  if (COMPACT)
+    grid.x = compact_grid(kernel, Shape::Cfg::kThreads, smem, dev, pl.num_ctas, p.persistent ? 1 : kCompactWaves, occ);
+  CUtensorMap kmap, vmap;
+  if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
+  e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
+  if (e != cudaSuccess) return fail_cuda(e, FP8 ? "fp8 partition kernel launch" : "partition kernel launch");
+  return 0;
+}
+
 template <typename T, int D>
 int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(pl.num_ctas));  // 1-D, sequence-major (cta_coords)
   cudaError_t e;
   if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
     if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
-      using Shape = TmaShapeFp8<D>;
-      static bool attr_done[kMaxDevices] = {false};
-      auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices>;
-      const int smem = Shape::Cfg::kSmemBytes;
-      e = ensure_smem_attr(kernel, smem, dev, attr_done);
-      if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(fp8 partition kernel)");
-      CUtensorMap kmap, vmap;
-      if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
-      e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
-      if (e != cudaSuccess) return fail_cuda(e, "fp8 partition kernel launch");
+      const int r = p.compact ? launch_tma<T, D, true, true>(a, pl, p, dev, stream)
+                              : launch_tma<T, D, true, false>(a, pl, p, dev, stream);
+      if (r) return r;
     } else {
       return fail(1, "internal: fp8 TMA path planned for head_dim %d", D);
     }
   } else if (pl.path == DK_PATH_TMA_MMA) {
-    using Shape = TmaShape<D>;
-    static bool attr_done[kMaxDevices] = {false};
-    auto kernel = paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps>;
-    const int smem = Shape::Cfg::kSmemBytes;
-    e = ensure_smem_attr(kernel, smem, dev, attr_done);
-    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(partition kernel)");
-    CUtensorMap kmap, vmap;
-    if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
-    e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
-    if (e != cudaSuccess) return fail_cuda(e, "partition kernel launch");
+    const int r = p.compact ? launch_tma<T, D, false, true>(a, pl, p, dev, stream)
+                            : launch_tma<T, D, false, false>(a, pl, p, dev, stream);
+    if (r) return r;
   } else if (p.kv_fp8) {
     auto kernel = paged_decode_simt_kernel<T, D, uint8_t>;
     e = launch_pdl(kernel, grid, dim3(kSimtThreads), SimtConfig<D>::kSmemBytes, stream, p);
@@ -636,6 +693,18 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.ws_partitions = pl.split ? a.max_partitions : 1;
   p.split = pl.split;
   p.kv_fp8 = a.kv_fp8;
+  // Compact grid (compact_coords) when most CTAs of the dense grid may have no
+  // tokens: many partitions per sequence, and few enough sequences that every
+  // CTA's warp scan of the lengths stays short.
+  // Compact grid (compact_coords): with DK_FLAG_PERSISTENT, and by default
+  // for e4m3 caches when a sequence may span many partitions.  Its CTAs pay a
+  // scan of the lengths (one L2 round trip) before their first loads; that
+  // is repaid where the consumers' math bounds a CTA (e4m3: c4 80.7 ->
+  // ~73 us) but not where HBM does (16-bit c4: 85 -> 89 us).
+  const bool persistent = (a.flags & DK_FLAG_PERSISTENT) != 0;
+  p.compact = pl.path == DK_PATH_TMA_MMA && a.num_seqs <= kCompactMaxSeqs &&
+              (persistent || (a.kv_fp8 && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1));
+  p.persistent = p.compact && persistent;
   p.scale_log2 = a.scale * (a.kv_fp8 ? a.k_scale : 1.0f) * kLog2e;
   p.v_scale = a.kv_fp8 ? a.v_scale : 1.0f;
   const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;

@@ -64,10 +64,16 @@ struct TmaConfig {
 // the consumers convert in registers (tile_math_fp8.cuh).  SLICES: 16-token
 // slices per consumer warp and tile (2: the warp's two slices share one
 // softmax update, for the e4m3 path whose consumers bound the throughput).
-template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false, int SLICES = 1>
-__global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(const __grid_constant__ CUtensorMap k_map,
-                                                                       const __grid_constant__ CUtensorMap v_map,
-                                                                       const DecodeParams p) {
+// MIN_CTAS: resident CTAs per SM the register allocation must allow (0: no
+// constraint, the compiler's own choice).  COMPACT: the grid is compact
+// (compact_coords) and a CTA runs items b, b + G, ..., carrying its ring
+// position and barrier phases from item to item; otherwise one CTA per
+// (partition, kv_head, seq) of the dense grid (cta_coords).
+template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false, int SLICES = 1, int MIN_CTAS = 0,
+          bool COMPACT = false>
+__global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
+    paged_decode_tma_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
+                            const DecodeParams p) {
   using Cfg = TmaConfig<D, NSTAGES, WARPS, FP8 ? 1 : 2, SLICES>;
   constexpr int TILE = Cfg::kTile;
   constexpr int H = Cfg::kHalves;
@@ -76,9 +82,11 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[NSTAGES];
   __shared__ __align__(8) uint64_t empty_bar[NSTAGES];
+  __shared__ int s_item[4];  // compact grid: seq (-1: no item), kv_head, partition, length
+  __shared__ int s_abort;    // compact grid: a bounded wait gave up, so run no further item
 
-  int part, kv_head, seq;
-  cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
+  int part = 0, kv_head = 0, seq = 0;
+  if constexpr (!COMPACT) cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rows_log2 = p.rows_log2;
@@ -93,6 +101,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
       mbar_init(&empty_bar[s], WARPS);
     }
     mbar_init_fence();
+    if constexpr (COMPACT) s_abort = 0;
   }
   if (warp == WARPS && lane == 0) {
     tma_prefetch_desc(&k_map);
@@ -105,108 +114,167 @@ __global__ void __launch_bounds__((WARPS + 1) * 32) paged_decode_tma_kernel(cons
 
   // Producer lane k (k < PAGES, the most pages a tile spans) addresses page k
   // of each tile and issues its box; lanes PAGES..2*PAGES-1 issue the V boxes
-  // of separate K/V caches.  The block ids of the first tile are fetched
+  // of separate K/V caches.  The block ids of an item's first tile are fetched
   // together with the length (entries below max_seq_len are inside the
   // block-table row), later ones one tile ahead.
   constexpr int PAGES = TILE / 8;  // block size >= 8 on this path
-  const int pstart = part * p.partition_size;
   const int kslot = lane % PAGES;
   const bool v_lane = lane >= PAGES && lane < 2 * PAGES && !p.kv_fused;
   const bool box_lane = warp == WARPS && (lane < PAGES || v_lane);
   const int bs_log2 = p.bs_log2;
   const int bs_mask = (1 << bs_log2) - 1;
-  const int* bt = p.block_tables + static_cast<int64_t>(seq) * p.bt_stride;
-  int pb = 0, off = 0;  // this lane's page of the next tile: block id and first row in the block
-  {
-    const int tok = pstart + (kslot << rows_log2);
-    if (box_lane && tok < p.max_seq_len) {
-      pb = __ldg(bt + (tok >> bs_log2));
-      off = tok & bs_mask;
+  float* red = reinterpret_cast<float*>(smem);  // merge scratch, over the ring once an item's tiles are read
+
+  // The tiles of one item (pstart < seq_len) and its result; g0 = tiles this
+  // CTA ran before it (ring position and barrier phases).
+  auto run_item = [&](int part, int kv_head, int seq, int seq_len, int pb, int off, uint32_t g0) {
+    const int pstart = part * p.partition_size;
+    const int pend = min(pstart + p.partition_size, seq_len);
+    const int ntiles = (pend - pstart + TILE - 1) / TILE;
+    if (warp == WARPS) {
+      // ------------------------------------------------------------------ producer
+      const int* bt = p.block_tables + static_cast<int64_t>(seq) * p.bt_stride;
+      const uint64_t policy = l2_evict_first_policy();
+      for (int t = 0; t < ntiles; ++t) {
+        const uint32_t u = g0 + t;
+        const int s = static_cast<int>(u % NSTAGES);
+        if (!mbar_wait(&empty_bar[s], ((u / NSTAGES) & 1) ^ 1)) {
+          if constexpr (COMPACT) s_abort = 1;
+          break;
+        }
+        const int tstart = pstart + t * TILE;
+        const int nops = (min(TILE, pend - tstart) + rows - 1) >> rows_log2;
+        if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(nops * page_bytes));
+        __syncwarp();  // the expected bytes are posted before any box can land
+        if (box_lane && kslot < nops) {
+          uint8_t* page = smem + s * Cfg::kStageBytes + kslot * page_bytes;
+          if (v_lane)
+            tma_load_5d(page + H * hstride, &v_map, 0, off, 0, kv_head, pb, &full_bar[s], policy);
+          else
+            tma_load_5d(page, &k_map, 0, off, 0, kv_head, pb, &full_bar[s], policy);
+        }
+        const int tok = tstart + TILE + (kslot << rows_log2);
+        if (box_lane && tok < pend) {
+          pb = __ldg(bt + (tok >> bs_log2));
+          off = tok & bs_mask;
+        }
+      }
+      pdl_launch_dependents();
+      // The producer then helps with the merge (it holds no partial state).
+      named_bar_sync(1, Cfg::kThreads);
+      named_bar_sync(1, Cfg::kThreads);
+      write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
+                                          [] { named_bar_sync(1, Cfg::kThreads); });
+      return;
     }
-  }
-
-  const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
-  if (pstart >= seq_len) {
-    // Empty sequence (single pass writes zeros) or a partition past the end
-    // (skipped; the merge kernel reads only live partitions).
-    if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
-    pdl_launch_dependents();
-    return;
-  }
-  const int pend = min(pstart + p.partition_size, seq_len);
-  const int ntiles = (pend - pstart + TILE - 1) / TILE;
-
-  if (warp == WARPS) {
-    // ------------------------------------------------------------------ producer
-    const uint64_t policy = l2_evict_first_policy();
+    // -------------------------------------------------------------------- consumers
+    using Tile = std::conditional_t<FP8, WarpAttentionFp8<T, D>, WarpAttention<T, D>>;
+    Tile wa;
+    wa.load_q_global(p, seq, kv_head, lane);
+    wa.reset();
+    float scale_log2 = p.scale_log2;
+    if constexpr (FP8) scale_log2 *= wa.q_scale;
+    const StageGeom<H> geom(rows_log2);
+    const int r0 = warp * kSubTokens * SLICES;  // first tile row of this warp
+    const uint32_t smem_base = smem_u32(smem);
     for (int t = 0; t < ntiles; ++t) {
-      const int s = t % NSTAGES;
-      if (!mbar_wait(&empty_bar[s], ((t / NSTAGES) & 1) ^ 1)) break;
-      const int tstart = pstart + t * TILE;
-      const int nops = (min(TILE, pend - tstart) + rows - 1) >> rows_log2;
-      if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], static_cast<uint32_t>(nops * page_bytes));
-      __syncwarp();  // the expected bytes are posted before any box can land
-      if (box_lane && kslot < nops) {
-        uint8_t* page = smem + s * Cfg::kStageBytes + kslot * page_bytes;
-        if (v_lane)
-          tma_load_5d(page + H * hstride, &v_map, 0, off, 0, kv_head, pb, &full_bar[s], policy);
-        else
-          tma_load_5d(page, &k_map, 0, off, 0, kv_head, pb, &full_bar[s], policy);
+      const uint32_t u = g0 + t;
+      const int s = static_cast<int>(u % NSTAGES);
+      const int sub0 = pstart + t * TILE + r0;  // first token of this warp's rows
+      // Only the last tile can start past this warp's rows.  Such a warp must
+      // not arrive on that stage's empty barrier here: with no full-barrier
+      // wait to hold it back, its arrival could count towards the pending
+      // phase of the tile NSTAGES earlier while a slower warp still reads that
+      // tile, and the producer would overwrite it.  (A CTA that runs another
+      // item arrives after this one, below.)
+      if (sub0 >= pend) break;
+      if (!mbar_wait(&full_bar[s], (u / NSTAGES) & 1)) {
+        if constexpr (COMPACT) s_abort = 1;
+        break;
       }
-      const int tok = tstart + TILE + (kslot << rows_log2);
-      if (box_lane && tok < pend) {
-        pb = __ldg(bt + (tok >> bs_log2));
-        off = tok & bs_mask;
-      }
+      if constexpr (SLICES == 2)
+        wa.slice2(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
+      else
+        wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
     pdl_launch_dependents();
-    // The producer then helps with the merge (it holds no partial state).
+    // Every tile's TMA writes have landed (warp 0 waits on every tile), so the
+    // ring can be reused for the cross-warp merge once all warps are here.
     named_bar_sync(1, Cfg::kThreads);
+    wa.to_red(red, WARPS, warp, p.group, lane);
     named_bar_sync(1, Cfg::kThreads);
-    float* red = reinterpret_cast<float*>(smem);
     write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
                                         [] { named_bar_sync(1, Cfg::kThreads); });
-    return;
-  }
+    if constexpr (COMPACT) {
+      // A warp with no rows in the last tile arrives on its empty barrier now,
+      // when every warp has finished reading the ring (the epilogue's
+      // barriers), so that the stage's phase completes before the next item.
+      if (lane == 0 && pstart + (ntiles - 1) * TILE + r0 >= pend)
+        mbar_arrive(&empty_bar[(g0 + ntiles - 1) % NSTAGES]);
+    }
+  };
 
-  // -------------------------------------------------------------------- consumers
-  using Tile = std::conditional_t<FP8, WarpAttentionFp8<T, D>, WarpAttention<T, D>>;
-  Tile wa;
-  wa.load_q_global(p, seq, kv_head, lane);
-  wa.reset();
-  float scale_log2 = p.scale_log2;
-  if constexpr (FP8) scale_log2 *= wa.q_scale;
-  const StageGeom<H> geom(rows_log2);
-  const int r0 = warp * kSubTokens * SLICES;  // first tile row of this warp
-  const uint32_t smem_base = smem_u32(smem);
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % NSTAGES;
-    const uint32_t parity = (t / NSTAGES) & 1;
-    const int sub0 = pstart + t * TILE + r0;  // first token of this warp's 16
-    // Only the last tile can start past this warp's rows.  Such a warp must
-    // not arrive on that stage's empty barrier: with no full-barrier wait to
-    // hold it back, its arrival could count towards the pending phase of the
-    // tile NSTAGES earlier while a slower warp still reads that tile, and the
-    // producer would overwrite it.  No one waits for the last tile's phase.
-    if (sub0 >= pend) break;
-    if (!mbar_wait(&full_bar[s], parity)) break;
-    if constexpr (SLICES == 2)
-      wa.slice2(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
-    else
-      wa.slice(smem_base + s * Cfg::kStageBytes, geom, r0, sub0, pend, scale_log2, lane);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
-  }
-  pdl_launch_dependents();
+  // The block ids of an item's first tile (producer lanes).
+  auto first_page = [&](int part, int seq, int& pb, int& off) {
+    const int tok = part * p.partition_size + (kslot << rows_log2);
+    if (box_lane && tok < p.max_seq_len) {
+      pb = __ldg(p.block_tables + static_cast<int64_t>(seq) * p.bt_stride + (tok >> bs_log2));
+      off = tok & bs_mask;
+    }
+  };
 
-  // Every tile's TMA writes have landed (warp 0 waits on every tile), so the
-  // ring can be reused for the cross-warp merge once all warps are here.
-  named_bar_sync(1, Cfg::kThreads);
-  float* red = reinterpret_cast<float*>(smem);
-  wa.to_red(red, WARPS, warp, p.group, lane);
-  named_bar_sync(1, Cfg::kThreads);
-  write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
-                                      [] { named_bar_sync(1, Cfg::kThreads); });
+  if constexpr (!COMPACT) {
+    int pb = 0, off = 0;  // this lane's page of the next tile: block id and first row in the block
+    first_page(part, seq, pb, off);
+    const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
+    if (part * p.partition_size >= seq_len) {
+      // Empty sequence (single pass writes zeros) or a partition past the end
+      // (skipped; the merge kernel reads only live partitions).
+      if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
+      pdl_launch_dependents();
+      return;
+    }
+    run_item(part, kv_head, seq, seq_len, pb, off, 0u);
+  } else {
+    uint32_t g0 = 0;
+    for (unsigned item = blockIdx.x;; item += gridDim.x) {
+      if (warp == 0) {
+        int len = 0;
+        const bool live = compact_coords(p, item, lane, part, kv_head, seq, len);
+        if (lane == 0) {
+          s_item[0] = live ? seq : -1;
+          s_item[1] = kv_head;
+          s_item[2] = part;
+          s_item[3] = len;
+        }
+      }
+      __syncthreads();
+      seq = s_item[0];
+      if (seq < 0) break;  // past the last item
+      kv_head = s_item[1];
+      part = s_item[2];
+      const int seq_len = s_item[3];
+      const int pstart = part * p.partition_size;
+      if (pstart >= seq_len) {
+        // an empty sequence's item
+        if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
+      } else {
+        int pb = 0, off = 0;
+        first_page(part, seq, pb, off);
+        run_item(part, kv_head, seq, seq_len, pb, off, g0);
+        g0 += (min(pstart + p.partition_size, seq_len) - pstart + TILE - 1) / TILE;
+      }
+      // The next item's TMA writes reuse the ring that the merge scratch
+      // occupied: order those generic accesses before them, and keep s_item
+      // until every thread has read it.
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (s_abort) break;
+    }
+    pdl_launch_dependents();
+  }
 }
 
 }  // namespace dkb

@@ -57,7 +57,10 @@ enum {
 /* Bits of DkPagedAttnArgs.flags. */
 enum {
   DK_FLAG_FORCE_SIMT = 1,        /* take the CUDA-core path even when the TMA path is eligible (testing) */
-  DK_FLAG_FORCE_FUSED_MERGE = 2  /* with merge counters, merge in the partition kernel whatever the merge size */
+  DK_FLAG_FORCE_FUSED_MERGE = 2, /* with merge counters, merge in the partition kernel whatever the merge size */
+  DK_FLAG_PERSISTENT = 4         /* TMA path, <= 512 sequences: one wave of CTAs, each running every G-th
+                                    live (sequence, KV head, partition) item; without it the live items
+                                    are numbered densely only when a sequence may span >= 16 partitions */
 };
 
 /* Limits shared with the Python wrapper. */
