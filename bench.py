@@ -374,28 +374,41 @@ def run_gpu_arm(args) -> None:
     # End to end through the public API with pinned host buffers, as a serving
     # loop runs it: every step copies its inputs (q, block tables, lengths)
     # host -> device and reads its output back device -> host.  The copies run
-    # on a copy stream into double buffers, so step i + 1's inputs and step
-    # i's output cross PCIe while step i's decode runs; the timed window spans
-    # the first input copy to the last output read.
-    h_q = q.cpu().pin_memory()
-    h_bt = kv.block_tables.cpu().pin_memory()
-    h_sl = kv.seq_lens.cpu().pin_memory()
-    h2d = h_q.numel() * h_q.element_size() + h_bt.numel() * 4 + h_sl.numel() * 4
+    # on two copy streams (one per direction: PCIe is full duplex) into double
+    # buffers, so step i + 1's inputs and step i - 1's output cross PCIe while
+    # step i's decode runs; the timed window spans the first input copy to the
+    # last output read.
+    # A step's inputs sit in one pinned staging buffer (q | block tables |
+    # lengths, each 256-byte aligned), as a serving loop prepares them, and
+    # cross PCIe in one copy; the device tensors are views of its copy.
+    parts = [q.contiguous(), kv.block_tables.contiguous(), kv.seq_lens.contiguous()]
+    offs, total = [], 0
+    for t in parts:
+        offs.append(total)
+        total += -(-t.numel() * t.element_size() // 256) * 256
+    h_stage = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    for t, o in zip(parts, offs):
+        nb = t.numel() * t.element_size()
+        h_stage[o:o + nb].copy_(t.view(-1).view(torch.uint8).cpu())
+    h2d = total  # bytes copied per step (the staging buffer, alignment padding included)
     d2h = out.numel() * out.element_size()
-    copy_stream = torch.cuda.Stream(dev)
-    ins = [(torch.empty_like(q), torch.empty_like(kv.block_tables), torch.empty_like(kv.seq_lens)) for _ in range(2)]
+    h2d_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
+    d_stage = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(2)]
+
+    def views(buf):
+        return tuple(buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t, o in zip(parts, offs))
+
+    ins = [views(d_stage[b]) for b in range(2)]
     outs = [torch.empty_like(out) for _ in range(2)]
     h_outs = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_comp = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def h2d_copy(b):  # on the copy stream
-        qd, btd, sld = ins[b]
-        qd.copy_(h_q, non_blocking=True)
-        btd.copy_(h_bt, non_blocking=True)
-        sld.copy_(h_sl, non_blocking=True)
-        ev_in[b].record(copy_stream)
+    def h2d_copy(b):  # on the host -> device stream
+        d_stage[b].copy_(h_stage, non_blocking=True)
+        ev_in[b].record(h2d_stream)
 
     def decode(b):  # on the compute stream
         qd, btd, sld = ins[b]
@@ -408,8 +421,9 @@ def run_gpu_arm(args) -> None:
 
     def e2e_run(nsteps, start_event=None):
         if start_event is not None:
-            copy_stream.wait_event(start_event)
-        with torch.cuda.stream(copy_stream):
+            h2d_stream.wait_event(start_event)
+            d2h_stream.wait_event(start_event)
+        with torch.cuda.stream(h2d_stream):
             h2d_copy(0)
         for i in range(nsteps):
             b = i % 2
@@ -420,15 +434,17 @@ def run_gpu_arm(args) -> None:
                 flush_buf.zero_()
             decode(b)
             ev_comp[b].record(stream)
-            with torch.cuda.stream(copy_stream):
-                if i + 1 < nsteps:
+            if i + 1 < nsteps:
+                with torch.cuda.stream(h2d_stream):
                     if i >= 1:
-                        copy_stream.wait_event(ev_comp[1 - b])  # step i - 1 no longer reads those inputs
+                        h2d_stream.wait_event(ev_comp[1 - b])  # step i - 1 no longer reads those inputs
                     h2d_copy(1 - b)
-                copy_stream.wait_event(ev_comp[b])
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(ev_comp[b])
                 h_outs[b].copy_(outs[b], non_blocking=True)
-                ev_out[b].record(copy_stream)
-        stream.wait_stream(copy_stream)
+                ev_out[b].record(d2h_stream)
+        stream.wait_stream(h2d_stream)
+        stream.wait_stream(d2h_stream)
 
     e2e_run(max(args.warmup, 3))
     e_steps = max(10, min(args.steps, 100))
@@ -511,8 +527,9 @@ def run_gpu_arm(args) -> None:
             },
             "e2e": {"value": kv_total / (e2e_s / e_steps) / 1e12, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e_steps, "api": "decodekernels_b200.paged_attention_decode",
-                    "copies": "pinned host buffers; each step's inputs H2D and output D2H on a copy stream, double "
-                              "buffered, overlapping the neighbouring steps' decode"},
+                    "copies": "pinned host buffers; each step's inputs (q, block tables, lengths in one staging "
+                              "buffer) H2D and its output D2H on one copy stream per direction, double buffered, "
+                              "overlapping the neighbouring steps' decode"},
             "gpu_launches": args.steps * (plan["launches"] + (1 if seq_mode else 0)),
             "exchange_errors": seq_attn.p2p_errors() if seq_mode else None,
             "with_gather": None if not gather_s else {
