@@ -201,6 +201,14 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
   return y;
 }
 
+// Both 16-bit halves of a register, e4m3x2 each -> f16x2: lo from bytes 0-1,
+// hi from bytes 2-3 (the halves are taken apart in PTX, no shift or mask).
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t four_bytes, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(four_bytes));
+}
+
 // Byte permute: result byte i = byte (sel >> 4i) & 7 of {b:a} (a = bytes 0-3).
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t y;

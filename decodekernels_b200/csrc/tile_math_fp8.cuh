@@ -100,15 +100,11 @@ struct WarpAttentionFp8 {
       ldmatrix_x4(r, k_base + (chunk >> 3) * g.hstride + (((chunk & 7) ^ sw) << 4));
       // bytes (4c, 4c+1) -> A register 0/1, bytes (4c+2, 4c+3) -> A register 2/3
       uint32_t a[4];
-      a[0] = e4m3x2_to_f16x2(r[0] & 0xFFFFu);
-      a[1] = e4m3x2_to_f16x2(r[1] & 0xFFFFu);
-      a[2] = e4m3x2_to_f16x2(r[0] >> 16);
-      a[3] = e4m3x2_to_f16x2(r[1] >> 16);
+      e4m3x4_to_f16x2x2(r[0], a[0], a[2]);
+      e4m3x4_to_f16x2x2(r[1], a[1], a[3]);
       Mma<__half>::run(sa, a, qf[kk][0], qf[kk][1]);
-      a[0] = e4m3x2_to_f16x2(r[2] & 0xFFFFu);
-      a[1] = e4m3x2_to_f16x2(r[3] & 0xFFFFu);
-      a[2] = e4m3x2_to_f16x2(r[2] >> 16);
-      a[3] = e4m3x2_to_f16x2(r[3] >> 16);
+      e4m3x4_to_f16x2x2(r[2], a[0], a[2]);
+      e4m3x4_to_f16x2x2(r[3], a[1], a[3]);
       Mma<__half>::run(sb2, a, qf[kk + 1][0], qf[kk + 1][1]);
     }
     float sc[4];
@@ -167,20 +163,12 @@ struct WarpAttentionFp8 {
       ldmatrix_x4_trans(r, v_base + (chunk >> 3) * g.hstride + (((chunk & 7) ^ sw) << 4));
       // r[i] bytes: (tok 2c, d 2g), (tok 2c, d 2g+1), (tok 2c+1, d 2g), (tok 2c+1, d 2g+1);
       // row g (d 2g) takes bytes 0 and 2, row g + 8 (d 2g+1) bytes 1 and 3
-      uint32_t x0 = prmt(r[0], 0u, 0x3120u);
-      uint32_t x1 = prmt(r[1], 0u, 0x3120u);  // tokens 8-15
       uint32_t a[4];
-      a[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
-      a[1] = e4m3x2_to_f16x2(x0 >> 16);
-      a[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
-      a[3] = e4m3x2_to_f16x2(x1 >> 16);
+      e4m3x4_to_f16x2x2(prmt(r[0], 0u, 0x3120u), a[0], a[1]);
+      e4m3x4_to_f16x2x2(prmt(r[1], 0u, 0x3120u), a[2], a[3]);  // tokens 8-15
       Mma<__half>::run(acc[mt], a, pb0, pb1);
-      x0 = prmt(r[2], 0u, 0x3120u);
-      x1 = prmt(r[3], 0u, 0x3120u);
-      a[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
-      a[1] = e4m3x2_to_f16x2(x0 >> 16);
-      a[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
-      a[3] = e4m3x2_to_f16x2(x1 >> 16);
+      e4m3x4_to_f16x2x2(prmt(r[2], 0u, 0x3120u), a[0], a[1]);
+      e4m3x4_to_f16x2x2(prmt(r[3], 0u, 0x3120u), a[2], a[3]);
       Mma<__half>::run(acc[mt + 1], a, pb0, pb1);
     }
   }
@@ -189,32 +177,20 @@ struct WarpAttentionFp8 {
   __device__ __forceinline__ static void k_frags(uint32_t addr, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
     uint32_t r[4];
     ldmatrix_x4(r, addr);
-    a0[0] = e4m3x2_to_f16x2(r[0] & 0xFFFFu);
-    a0[1] = e4m3x2_to_f16x2(r[1] & 0xFFFFu);
-    a0[2] = e4m3x2_to_f16x2(r[0] >> 16);
-    a0[3] = e4m3x2_to_f16x2(r[1] >> 16);
-    a1[0] = e4m3x2_to_f16x2(r[2] & 0xFFFFu);
-    a1[1] = e4m3x2_to_f16x2(r[3] & 0xFFFFu);
-    a1[2] = e4m3x2_to_f16x2(r[2] >> 16);
-    a1[3] = e4m3x2_to_f16x2(r[3] >> 16);
+    e4m3x4_to_f16x2x2(r[0], a0[0], a0[2]);
+    e4m3x4_to_f16x2x2(r[1], a0[1], a0[3]);
+    e4m3x4_to_f16x2x2(r[2], a1[0], a1[2]);
+    e4m3x4_to_f16x2x2(r[3], a1[1], a1[3]);
   }
 
   // V chunk pair mt, mt + 1 of one 16-row slice -> row-permuted V^T A fragments.
   __device__ __forceinline__ static void v_frags(uint32_t addr, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
     uint32_t r[4];
     ldmatrix_x4_trans(r, addr);
-    uint32_t x0 = prmt(r[0], 0u, 0x3120u);
-    uint32_t x1 = prmt(r[1], 0u, 0x3120u);
-    a0[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
-    a0[1] = e4m3x2_to_f16x2(x0 >> 16);
-    a0[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
-    a0[3] = e4m3x2_to_f16x2(x1 >> 16);
-    x0 = prmt(r[2], 0u, 0x3120u);
-    x1 = prmt(r[3], 0u, 0x3120u);
-    a1[0] = e4m3x2_to_f16x2(x0 & 0xFFFFu);
-    a1[1] = e4m3x2_to_f16x2(x0 >> 16);
-    a1[2] = e4m3x2_to_f16x2(x1 & 0xFFFFu);
-    a1[3] = e4m3x2_to_f16x2(x1 >> 16);
+    e4m3x4_to_f16x2x2(prmt(r[0], 0u, 0x3120u), a0[0], a0[1]);
+    e4m3x4_to_f16x2x2(prmt(r[1], 0u, 0x3120u), a0[2], a0[3]);
+    e4m3x4_to_f16x2x2(prmt(r[2], 0u, 0x3120u), a1[0], a1[1]);
+    e4m3x4_to_f16x2x2(prmt(r[3], 0u, 0x3120u), a1[2], a1[3]);
   }
 
   // Two 16-token slices (tile rows r0..r0+31, first token sub0) with one
