@@ -13,6 +13,7 @@ The kernels live in ``libdk_b200.so`` (C ABI: ``include/dk_paged_attention.h``);
 """
 
 from .ops import (
+    FLAG_PERSISTENT,
     MAX_GQA_GROUP,
     PARTITION_SIZE,
     SUPPORTED_HEAD_DIMS,
@@ -26,6 +27,7 @@ from .ops import (
 )
 
 __all__ = [
+    "FLAG_PERSISTENT",
     "MAX_GQA_GROUP",
     "PARTITION_SIZE",
     "SUPPORTED_HEAD_DIMS",
@@ -37,4 +39,4 @@ __all__ = [
     "paged_attention_decode_lse",
     "reshape_and_cache",
 ]
-__version__ = "0.4.0"
+__version__ = "0.5.0"

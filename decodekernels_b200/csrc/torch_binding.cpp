@@ -50,7 +50,7 @@ std::string workspace_problem(const at::Tensor& tmp_out, const at::Tensor& max_l
 void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                  const at::Tensor& block_tables, const at::Tensor& seq_lens, double scale, int64_t max_seq_len,
                  at::Tensor& tmp_out, at::Tensor& max_logits, at::Tensor& exp_sums, at::Tensor* merge_counters,
-                 at::Tensor* partial = nullptr, double k_scale = 1.0, double v_scale = 1.0) {
+                 at::Tensor* partial = nullptr, double k_scale = 1.0, double v_scale = 1.0, int64_t flags = 0) {
   TORCH_CHECK(q.is_cuda(), "paged_attention_decode: q must be a CUDA tensor");
   TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4,
               "k_cache and v_cache must be [num_blocks, block_size, num_kv_heads, head_dim]");
@@ -169,7 +169,9 @@ void decode_impl(at::Tensor& out, const at::Tensor& q, const at::Tensor& k_cache
   a.max_partitions = max_partitions;
   a.partition_size = 0;
   a.dtype = q.scalar_type() == at::kBFloat16 ? DK_DTYPE_BFLOAT16 : DK_DTYPE_FLOAT16;
-  a.flags = 0;
+  TORCH_CHECK(flags >= 0 && flags <= (DK_FLAG_FORCE_SIMT | DK_FLAG_FORCE_FUSED_MERGE | DK_FLAG_PERSISTENT),
+              "paged_attention_decode: unknown flags ", flags);
+  a.flags = static_cast<int32_t>(flags);
   a.scale = static_cast<float>(scale);
   a.kv_fp8 = kv_fp8 ? 1 : 0;
   a.k_scale = static_cast<float>(k_scale);
@@ -219,10 +221,10 @@ void paged_attention_decode_ext(at::Tensor& out, const at::Tensor& q, const at::
                                 const at::Tensor& v_cache, const at::Tensor& block_tables, const at::Tensor& seq_lens,
                                 double scale, int64_t max_seq_len, at::Tensor& tmp_out, at::Tensor& max_logits,
                                 at::Tensor& exp_sums, const c10::optional<at::Tensor>& merge_counters, double k_scale,
-                                double v_scale) {
+                                double v_scale, int64_t flags) {
   at::Tensor counters = merge_counters.has_value() ? *merge_counters : at::Tensor();
   decode_impl(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
-              counters.defined() ? &counters : nullptr, nullptr, k_scale, v_scale);
+              counters.defined() ? &counters : nullptr, nullptr, k_scale, v_scale, flags);
 }
 
 // Merge partials [R, n, Hq, D + 4] (disjoint token ranges) into out: the
@@ -336,7 +338,7 @@ TORCH_LIBRARY(decode_kernels, m) {
   m.def(
       "paged_attention_decode_ext(Tensor! out, Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, "
       "Tensor seq_lens, float scale, int max_seq_len, Tensor! tmp_out, Tensor! max_logits, Tensor! exp_sums, "
-      "Tensor(a!)? merge_counters, float k_scale, float v_scale) -> ()");
+      "Tensor(a!)? merge_counters, float k_scale, float v_scale, int flags=0) -> ()");
   m.def("merge_lse(Tensor! out, Tensor parts) -> ()");
   m.def(
       "reshape_and_cache(Tensor key, Tensor value, Tensor! key_cache, Tensor! value_cache, Tensor slot_mapping, "

@@ -38,6 +38,7 @@ from . import capi
 PARTITION_SIZE = 512  # the reference's split-K partition; the workspace is never smaller than its ceil(L / 512)
 MAX_GQA_GROUP = capi.DK_MAX_GQA_GROUP
 SUPPORTED_HEAD_DIMS = (64, 128, 256)
+FLAG_PERSISTENT = capi.DK_FLAG_PERSISTENT  # one wave of CTAs over the live work items
 
 TORCH_LIB_PATH = Path(__file__).resolve().parent / "lib" / "libdk_b200_torch.so"
 
@@ -64,7 +65,7 @@ def _register_fakes() -> None:
 
     @torch.library.register_fake("decode_kernels::paged_attention_decode_ext")
     def _(out, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, tmp_out, max_logits, exp_sums,
-          merge_counters, k_scale, v_scale):
+          merge_counters, k_scale, v_scale, flags=0):
         return None
 
     @torch.library.register_fake("decode_kernels::merge_lse")
@@ -157,6 +158,7 @@ def paged_attention_decode(
     workspace: tuple | None = None,
     k_scale: float = 1.0,
     v_scale: float = 1.0,
+    flags: int = 0,
 ) -> torch.Tensor:
     """Single-token decode attention over a paged KV cache.
 
@@ -168,6 +170,10 @@ def paged_attention_decode(
 
     Caches of dtype uint8 / float8_e4m3fn hold e4m3 codes (as written by
     :func:`reshape_and_cache`): K = code * k_scale, V = code * v_scale.
+    ``flags``: ``DK_FLAG_*`` bits of the C ABI (``capi.DK_FLAG_PERSISTENT``:
+    one wave of CTAs over the live work items, for a grid planned from a
+    large ``max_seq_len`` such as a CUDA graph captured for a model's
+    maximum length).
     """
     _require()
     num_seqs, num_q_heads, head_dim = q.shape
@@ -184,10 +190,10 @@ def paged_attention_decode(
                                     block_size=bs)
     tmp_out, max_logits, exp_sums = workspace[:3]
     counters = workspace[3] if len(workspace) > 3 else None
-    if k_cache.dtype in (torch.uint8, torch.float8_e4m3fn):
+    if flags or k_cache.dtype in (torch.uint8, torch.float8_e4m3fn):
         torch.ops.decode_kernels.paged_attention_decode_ext(
             out, q, k_cache, v_cache, block_tables, seq_lens, float(scale), int(max_seq_len), tmp_out, max_logits,
-            exp_sums, counters, float(k_scale), float(v_scale)
+            exp_sums, counters, float(k_scale), float(v_scale), int(flags)
         )
     elif counters is not None:
         torch.ops.decode_kernels.paged_attention_decode_fused(

@@ -19,12 +19,20 @@ backend):
   ``layer._k_scale_float`` / ``layer._v_scale_float``, as long as the query
   stays 16-bit.  The reference refuses every quantized cache
   (``decode_kernels/vllm_patch.py:74``); this library has an e4m3 path.
+* CUDA-graph capture (vLLM's full-cudagraph mode) is served too, where the
+  reference refused it (``decode_kernels/vllm_patch.py:65-69``): vLLM builds
+  the metadata it captures with ``max_seq_len = max_model_len``
+  (``v1/worker/gpu_model_runner.py``, ``for_cudagraph_capture``), a bound on
+  every replay's lengths, and refreshes ``seq_lens`` and ``block_table`` in
+  place before each replay, which the kernels read on the device.  A grid
+  planned for the model's maximum length is mostly empty at replay, so a
+  captured call takes the persistent grid (``FLAG_PERSISTENT``: one wave of
+  CTAs over the live work items).
 * Everything else falls back to the original FlashAttention path through a
   strict eligibility check (``_attention_eligible``): prefill and mixed
   batches, e5m2 or other quantized caches, fp8 queries, sliding windows,
   ALiBi, soft-capping, sinks, cascade attention, context parallelism,
-  CUDA-graph capture, head sizes other than 64/128/256 and GQA groups
-  above 8.
+  head sizes other than 64/128/256 and GQA groups above 8.
 * ``rms_norm`` and ``silu_and_mul`` (the reference's other two patches) are
   not part of this library; asking for them logs a note and changes nothing.
 """
@@ -74,10 +82,6 @@ def _attention_eligible(impl, query, kv_cache, attn_metadata, output, output_sca
                         layer=None) -> bool:
     """True when this decode batch can run on decodekernels_b200 unchanged."""
     if attn_metadata is None or output_scale is not None or output_block_scale is not None:
-        return False
-    if query.is_cuda and torch.cuda.is_current_stream_capturing():
-        # The split-K grid is planned from the host-side max_seq_len; leave
-        # captured graphs to FlashAttention, as the reference does.
         return False
     try:
         from vllm.v1.attention.backend import AttentionType
@@ -132,9 +136,12 @@ def _decode(impl, query, kv_cache, attn_metadata, output, layer=None) -> torch.T
     k_scale, v_scale = 1.0, 1.0
     if str(getattr(impl, "kv_cache_dtype", "auto")) in _FP8_E4M3:
         k_scale, v_scale = _fp8_scales(layer)
+    # Under capture the grid is planned from max_seq_len (vLLM passes the
+    # model's maximum length) and replayed with other lengths: persistent grid.
+    flags = dk_ops.FLAG_PERSISTENT if query.is_cuda and torch.cuda.is_current_stream_capturing() else 0
     dk_ops.paged_attention_decode(q, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
                                   scale=impl.scale, max_seq_len=attn_metadata.max_seq_len, out=out, k_scale=k_scale,
-                                  v_scale=v_scale)
+                                  v_scale=v_scale, flags=flags)
     return output
 
 
