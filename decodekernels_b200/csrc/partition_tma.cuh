@@ -1,15 +1,16 @@
 // Partition kernel, sm_100a fast path: TMA-staged KV pages + tensor-core math.
 //
-// One CTA per (partition, kv_head, seq) computes all `group` query heads of
-// its KV head, so every K/V byte is read from HBM once (DecodeKernels'
-// GQA-aware block, csrc/paged_attention.cuh:73-225, re-designed):
+// One CTA per (partition, kv_head, seq) work item computes all `group` query
+// heads of its KV head, so every K/V byte is read from HBM once
+// (DecodeKernels' GQA-aware block, csrc/paged_attention.cuh:73-225,
+// re-designed):
 //
-// * Warp WARPS (producer) reads the partition's block-table slice (32 entries per
-//   coalesced load, the next group prefetched) and, per tile, issues
-//   ONE 5-D TMA box per page for K and one for V -- or a single box for both
-//   when the cache is vLLM's interleaved K|V buffer -- into an NSTAGES-deep
-//   shared-memory ring.  The tensor maps are (64 columns, token, 64-column
-//   block, head, block) with the caches' real strides, so the vLLM and
+// * Warp WARPS (producer): lane k addresses page k of every tile -- it loads
+//   that page's block id itself, one tile ahead -- and issues ONE 5-D TMA box
+//   per page for K (lanes PAGES.. for V) -- or a single box for both when the
+//   cache is vLLM's interleaved K|V buffer -- into an NSTAGES-deep
+//   shared-memory ring.  The tensor maps are (128 bytes of columns, token,
+//   column block, head, block) with the caches' real strides, so the vLLM and
 //   FlashInfer NHD/HND views are read in place, and a box lands as
 //   [column block][page row][128 B], 128-byte swizzled.  Block-size arithmetic
 //   is shifts (power-of-two block sizes only on this path).  Block ids outside
