@@ -352,21 +352,25 @@ def run_gpu_arm(args) -> None:
         sampler.stop()
 
     # With N GPUs, also time the variant whose consumer needs every head on
-    # every rank: decode + NCCL all-gather of the per-head outputs.
+    # every rank: decode + all-gather of the per-head outputs (our NVLink
+    # peer-memory kernel, or NCCL with --exchange nccl).
     gather_s = None
+    gatherer = None
     if world > 1 and not seq_mode:
-        from decodekernels_b200.sharded import gather_heads, head_shard
+        from decodekernels_b200.sharded import ShardedPagedAttention
 
-        shard = head_shard(batch.config.num_q_heads, batch.config.num_kv_heads, rank, world)
+        gatherer = ShardedPagedAttention(batch.config.num_q_heads, batch.config.num_kv_heads, rank, world,
+                                         exchange=args.exchange)
+        full_out = torch.empty(out.shape[0], batch.config.num_q_heads, out.shape[2], dtype=out.dtype, device=dev)
         for _ in range(3):
-            gather_heads(out, shard)
+            gatherer.gather(out, full_out)
         torch.distributed.barrier()
         torch.cuda.synchronize()
         gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         gs.record(stream)
         for _ in range(args.steps):
             step()
-            gather_heads(out, shard)
+            gatherer.gather(out, full_out)
         ge.record(stream)
         torch.cuda.synchronize()
         gather_s = gs.elapsed_time(ge) * 1e-3
@@ -531,10 +535,12 @@ def run_gpu_arm(args) -> None:
                               "buffer) H2D and its output D2H on one copy stream per direction, double buffered, "
                               "overlapping the neighbouring steps' decode"},
             "gpu_launches": args.steps * (plan["launches"] + (1 if seq_mode else 0)),
-            "exchange_errors": seq_attn.p2p_errors() if seq_mode else None,
+            "exchange_errors": (seq_attn.p2p_errors() if seq_mode
+                                else gatherer.p2p_errors() if gatherer is not None else None),
             "with_gather": None if not gather_s else {
                 "us_per_call": gather_s / args.steps * 1e6, "value": kv_total / (gather_s / args.steps) / 1e12,
-                "unit": UNIT, "note": "decode + NCCL all-gather of the per-head outputs to every rank"},
+                "unit": UNIT, "note": "decode + all-gather of the per-head outputs to every rank ("
+                + ("one NVLink peer-memory kernel, dk_gather_heads)" if args.exchange == "p2p" else "NCCL)")},
             "clocks": sampler.summary(t0, t1) if sampler else None,
             "wall_s_timed": t1 - t0,
         }
@@ -558,8 +564,9 @@ def main() -> None:
     ap.add_argument("--workload", default="c5",
                     choices=["c1", "c2", "c3", "c4", "c5", "c2f8", "c3f8", "c4f8", "c5f8"])
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
-                    help="sequence sharding: partial rows pushed over NVLink peer memory (one kernel) or an NCCL "
-                         "all-gather followed by the merge kernel")
+                    help="N>1: the collective over NVLink peer memory (one kernel of ours) or NCCL; sequence "
+                         "sharding: the partial rows' exchange + merge, head sharding: the all-gather of the "
+                         "per-head outputs timed beside the decode (with_gather)")
     ap.add_argument("--sharding", default="auto", choices=["auto", "head", "seq"],
                     help="N>1: KV-head sharding (no exchange) or block-striped sequence sharding (partials "
                          "all-gathered and merged every step); auto = head when the KV heads divide evenly")

@@ -33,7 +33,7 @@ DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
             "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache",
-            "dk_paged_attention_decode_lse", "dk_merge_lse", "dk_exchange_merge_lse")
+            "dk_paged_attention_decode_lse", "dk_merge_lse", "dk_exchange_merge_lse", "dk_gather_heads")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -144,6 +144,27 @@ class DkPeerExchangeArgs(ctypes.Structure):
     ]
 
 
+class DkPeerGatherArgs(ctypes.Structure):
+    _fields_ = [
+        ("local", ctypes.c_void_p),
+        ("local_stride_seq", ctypes.c_int64),
+        ("local_stride_head", ctypes.c_int64),
+        ("recv", ctypes.c_void_p * DK_MAX_PEERS),
+        ("flags", ctypes.c_void_p * DK_MAX_PEERS),
+        ("state", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_stride_seq", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("num_seqs", ctypes.c_int32),
+        ("heads_per_rank", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("wait_limit_ms", ctypes.c_uint32),
+    ]
+
+
 class DkPlan(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int32),
@@ -197,6 +218,8 @@ def load() -> ctypes.CDLL:
         lib.dk_merge_lse.restype = ctypes.c_int
         lib.dk_exchange_merge_lse.argtypes = [ctypes.POINTER(DkPeerExchangeArgs), ctypes.c_void_p]
         lib.dk_exchange_merge_lse.restype = ctypes.c_int
+        lib.dk_gather_heads.argtypes = [ctypes.POINTER(DkPeerGatherArgs), ctypes.c_void_p]
+        lib.dk_gather_heads.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -403,6 +426,32 @@ def merge_lse(parts, out, stream=None) -> int:
     rc = load().dk_merge_lse(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_merge_lse failed ({rc}): {last_error()}")
+    return rc
+
+
+def gather_heads(local, recv_ptrs, flag_ptrs, state, out, rank: int, world: int, wait_limit_ms: int = 0,
+                 stream=None) -> int:
+    """dk_gather_heads: push ``local`` [n, Hq / world, D] (this rank's heads)
+    to every GPU's receive buffer, wait for every rank's flag, copy all heads
+    into ``out`` [n, Hq, D]."""
+    import torch
+
+    a = DkPeerGatherArgs()
+    a.local, a.local_stride_seq, a.local_stride_head = local.data_ptr(), local.stride(0), local.stride(1)
+    for r in range(world):
+        a.recv[r] = recv_ptrs[r]
+        a.flags[r] = flag_ptrs[r]
+    a.state = state.data_ptr()
+    a.out, a.out_stride_seq, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.rank, a.world = rank, world
+    a.num_seqs, a.heads_per_rank, a.head_dim = local.shape[0], local.shape[1], local.shape[2]
+    a.dtype = _dtype_code(out)
+    a.wait_limit_ms = wait_limit_ms
+    if stream is None:
+        stream = torch.cuda.current_stream(local.device).cuda_stream
+    rc = load().dk_gather_heads(ctypes.byref(a), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_gather_heads failed ({rc}): {last_error()}")
     return rc
 
 

@@ -29,7 +29,7 @@
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 600;  // 0.6.0: dk_exchange_merge_lse; 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
+constexpr int kVersion = 700;  // 0.7.0: dk_gather_heads, DK_FLAG_PERSISTENT; 0.6.0: dk_exchange_merge_lse; 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
                                 // dk_paged_attention_decode_lse / dk_merge_lse; 0.3.0: dk_reshape_and_cache;
                                 // 0.2.0: DkPagedAttnArgs.merge_counters
 // Planner: partitions are sized so that the grid is about one wave of
@@ -853,6 +853,58 @@ int launch_peer_exchange(const DkPeerExchangeArgs& a, int dev, cudaStream_t stre
   return e == cudaSuccess ? 0 : fail_cuda(e, "peer exchange kernel launch");
 }
 
+int validate_peer_gather(const DkPeerGatherArgs* a) {
+  if (a == nullptr) return fail(1, "dk_gather_heads: args is NULL");
+  if (a->world < 1 || a->world > DK_MAX_PEERS || a->rank < 0 || a->rank >= a->world)
+    return fail(1, "dk_gather_heads: need 0 <= rank < world <= %d", DK_MAX_PEERS);
+  if (a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return fail(1, "head_dim must be 64, 128 or 256, got %d", a->head_dim);
+  if (a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
+    return fail(1, "dk_gather_heads: dtype must be float16 or bfloat16 (code %d)", a->dtype);
+  if (a->num_seqs < 0 || a->heads_per_rank <= 0) return fail(1, "dk_gather_heads: bad sizes");
+  if (!a->local || !a->state || !a->out) return fail(1, "dk_gather_heads: NULL pointer");
+  if (!aligned(a->local, 16) || !aligned(a->out, 16) || a->local_stride_seq % 8 || a->local_stride_head % 8 ||
+      a->out_stride_seq % 8 || a->out_stride_head % 8)
+    return fail(1, "dk_gather_heads: local and out rows must start on 16-byte boundaries");
+  for (int r = 0; r < a->world; ++r) {
+    if (!a->recv[r] || !a->flags[r]) return fail(1, "dk_gather_heads: NULL peer pointer for rank %d", r);
+    if (!aligned(a->recv[r], 16) || !aligned(a->flags[r], 4))
+      return fail(1, "dk_gather_heads: receive buffers must be 16-byte aligned");
+  }
+  return 0;
+}
+
+int launch_peer_gather(const DkPeerGatherArgs& a, int dev, cudaStream_t stream) {
+  PeerGatherParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.local = static_cast<const uint16_t*>(a.local);
+  p.local_stride_seq = a.local_stride_seq;
+  p.local_stride_head = a.local_stride_head;
+  for (int r = 0; r < a.world; ++r) {
+    p.recv[r] = static_cast<uint16_t*>(a.recv[r]);
+    p.flags[r] = a.flags[r];
+  }
+  p.state = a.state;
+  p.out = static_cast<uint16_t*>(a.out);
+  p.out_stride_seq = a.out_stride_seq;
+  p.out_stride_head = a.out_stride_head;
+  p.num_seqs = a.num_seqs;
+  p.heads_per_rank = a.heads_per_rank;
+  p.num_q_heads = a.heads_per_rank * a.world;
+  p.head_dim = a.head_dim;
+  p.slot_elems = static_cast<int64_t>(a.num_seqs) * p.num_q_heads * a.head_dim;
+  p.rank = a.rank;
+  p.world = a.world;
+  p.wait_limit_ns = (a.wait_limit_ms ? a.wait_limit_ms : 2000u) * 1000000ull;
+  // at most two CTAs per SM: every CTA must be resident while they wait on one another's flags
+  const long long chunks = p.slot_elems / 8;
+  const long long want = std::max<long long>(1, (chunks + kExchangeThreads - 1) / kExchangeThreads);
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(want, 2LL * num_sms(dev))));
+  peer_gather_kernel<<<grid, kExchangeThreads, 0, stream>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail_cuda(e, "peer gather kernel launch");
+}
+
 // ---------------------------------------------------------------------------
 // Paged-KV write
 // ---------------------------------------------------------------------------
@@ -1074,6 +1126,14 @@ int dk_exchange_merge_lse(const DkPeerExchangeArgs* args, dk_stream_t stream) {
     default:
       return dkb::launch_peer_exchange<256>(*args, dev, s);
   }
+}
+
+int dk_gather_heads(const DkPeerGatherArgs* args, dk_stream_t stream) {
+  if (int e = dkb::validate_peer_gather(args)) return e;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  return dkb::launch_peer_gather(*args, dev, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int dk_reshape_and_cache(const DkCacheWriteArgs* args, dk_stream_t stream) {

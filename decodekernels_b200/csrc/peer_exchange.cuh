@@ -150,4 +150,102 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_merge_kernel(c
   }
 }
 
+// All-gather of KV-head shards over NVLink peer memory, one kernel per GPU:
+// rank r holds the attention output of query heads [r * hpr, (r + 1) * hpr)
+// ([n, hpr, D], strided) and every rank needs all heads [n, Hq, D].  The same
+// protocol as peer_exchange_merge_kernel, with a copy instead of the merge:
+//
+//   1. push: this rank's rows into slot (e % 2) of every rank's receive
+//      buffer [2][n, Hq, D] at heads [rank * hpr, ...) (16-byte peer stores);
+//   2. publish: the last CTA to finish pushing fences at system scope and
+//      stores e into this rank's flag on every GPU (release, system scope);
+//   3. wait: every CTA waits (bounded by wait_limit_ns; a give-up is counted
+//      in the error word) until every rank's flag on this GPU reached e;
+//   4. copy the complete slot into `out` (any seq / head strides);
+//   5. the last CTA to finish advances the call counter.
+//
+// Slot (e + 1) % 2 is free when a peer pushes call e + 1 into it for the same
+// reason as in the exchange: its last reader, this GPU's copy of call e - 1,
+// finished before this GPU published e.  Elements move as opaque 16-bit
+// values in 16-byte chunks (rows of D = 64, 128 or 256 elements).
+struct PeerGatherParams {
+  const uint16_t* local;  // this rank's heads [n, hpr, D]
+  int64_t local_stride_seq, local_stride_head;
+  uint16_t* recv[kMaxPeers];  // every rank's receive buffers [2][n, Hq, D]
+  uint32_t* flags[kMaxPeers];
+  uint32_t* state;  // this GPU: [0] completed calls, [1] pushers done, [2] copiers done, [3] errors
+  uint16_t* out;    // [n, Hq, D]
+  int64_t out_stride_seq, out_stride_head;
+  int64_t slot_elems;  // n * Hq * D
+  int rank, world, num_seqs, num_q_heads, heads_per_rank, head_dim;
+  unsigned long long wait_limit_ns;
+};
+
+__global__ void __launch_bounds__(kExchangeThreads) peer_gather_kernel(const PeerGatherParams p) {
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_last;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_epoch = p.state[0] + 1;  // nothing advances state[0] before every CTA has copied
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int64_t par_off = static_cast<int64_t>(e & 1u) * p.slot_elems;
+  const int chunks = p.head_dim >> 3;  // 16-byte chunks per row
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kExchangeThreads;
+
+  // 1. push this rank's rows into slot (e % 2) of every rank
+  const int64_t mine = static_cast<int64_t>(p.num_seqs) * p.heads_per_rank * chunks;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExchangeThreads + tid; i < mine; i += stride) {
+    const int64_t row = i / chunks;
+    const int c = static_cast<int>(i - row * chunks);
+    const int64_t seq = row / p.heads_per_rank;
+    const int h = static_cast<int>(row - seq * p.heads_per_rank);
+    const uint4 v = *reinterpret_cast<const uint4*>(p.local + seq * p.local_stride_seq + h * p.local_stride_head + c * 8);
+    const int64_t dst = par_off + (seq * p.num_q_heads + p.rank * p.heads_per_rank + h) * p.head_dim + c * 8;
+    for (int r = 0; r < p.world; ++r) *reinterpret_cast<uint4*>(p.recv[r] + dst) = v;
+  }
+  // 2. publish: the last CTA to finish pushing sets this rank's flag everywhere
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&p.state[1], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (tid == 0) __threadfence_system();
+    __syncthreads();
+    if (tid < p.world) st_release_sys(p.flags[tid] + p.rank, e);
+    if (tid == 0) p.state[1] = 0;
+  }
+  // 3. wait for every rank's flag on this GPU
+  if (tid == 0) {
+    const unsigned long long t0 = global_timer_ns();
+    for (int r = 0; r < p.world; ++r) {
+      while (static_cast<int32_t>(ld_acquire_sys(p.flags[p.rank] + r) - e) < 0) {
+        if (global_timer_ns() - t0 > p.wait_limit_ns) {
+          atomicAdd(&p.state[3], 1u);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // 4. copy the gathered slot into out
+  const uint16_t* slot = p.recv[p.rank] + par_off;
+  const int64_t all = static_cast<int64_t>(p.num_seqs) * p.num_q_heads * chunks;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExchangeThreads + tid; i < all; i += stride) {
+    const int64_t row = i / chunks;
+    const int c = static_cast<int>(i - row * chunks);
+    const int64_t seq = row / p.num_q_heads;
+    const int h = static_cast<int>(row - seq * p.num_q_heads);
+    const int4 v = __ldcg(reinterpret_cast<const int4*>(slot + row * p.head_dim + c * 8));  // peers wrote it
+    *reinterpret_cast<int4*>(p.out + seq * p.out_stride_seq + h * p.out_stride_head + c * 8) = v;
+  }
+  // 5. the last CTA to finish advances the call counter
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&p.state[2], 1u) == gridDim.x - 1) {
+    p.state[2] = 0;
+    p.state[0] = e;
+  }
+}
+
 }  // namespace dkb

@@ -10,9 +10,11 @@ Attention is independent per KV head, and KV head ``h`` owns query heads
 ``[num_blocks, bs, Hkv/G, D]`` cache), the matching query heads and the
 matching slice of the output.  Block tables and lengths are replicated.  No
 data moves between ranks to compute a rank's heads, so a head-sharded
-consumer (a tensor-parallel o_proj) needs no collective at all; an NCCL
+consumer (a tensor-parallel o_proj) needs no collective at all; an
 all-gather of the per-head outputs is offered only for consumers that need
-every head on every rank (``gather=True``).
+every head on every rank (``gather=True``): NCCL's, or one kernel of ours
+that stores each rank's heads into every peer's memory over NVLink
+(``exchange="p2p"``, ``dk_gather_heads``).
 
 Sequence sharding, for models whose KV heads cannot be split (MQA, or
 fewer KV heads than GPUs) and for long contexts at small batch: block ``j``
@@ -106,11 +108,16 @@ class ShardedPagedAttention:
 
     ``attention_fn`` defaults to :func:`decodekernels_b200.paged_attention_decode`
     (the sm_100a kernels); tests of the host-side logic on CPU ranks pass the
-    CPU oracle instead.
+    CPU oracle instead.  ``exchange`` chooses the gather: ``"nccl"``
+    (``all_gather_into_tensor``) or ``"p2p"`` (``dk_gather_heads`` over
+    symmetric memory; CUDA ranks of one node, waits bounded by
+    ``wait_limit_ms``, 0 = 2 s).
     """
 
+    _FLAG_BYTES = 256  # flag words at the head of each rank's symmetric buffer
+
     def __init__(self, num_q_heads: int, num_kv_heads: int, rank: int | None = None, world: int | None = None,
-                 group=None, attention_fn: Callable | None = None):
+                 group=None, attention_fn: Callable | None = None, exchange: str = "nccl", wait_limit_ms: int = 0):
         import torch.distributed as dist
 
         if rank is None or world is None:
@@ -118,16 +125,47 @@ class ShardedPagedAttention:
                 rank, world = dist.get_rank(group), dist.get_world_size(group)
             else:
                 rank, world = 0, 1
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', got {exchange!r}")
         self.shard = head_shard(num_q_heads, num_kv_heads, rank, world)
         self.group = group
+        self.exchange = exchange
+        self.wait_limit_ms = wait_limit_ms
+        self._p2p = None
         if attention_fn is None:
             from .ops import paged_attention_decode
 
             attention_fn = paged_attention_decode
         self.attention_fn = attention_fn
 
+    def _p2p_buffers(self, slot_bytes: int, device):
+        """Symmetric allocation (collective on first use, or when a larger batch
+        needs more room): every rank's [flags | 2 receive slots]."""
+        if self._p2p is not None and self._p2p[0] >= slot_bytes:
+            return self._p2p
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        group = self.group if self.group is not None else dist.group.WORLD
+        buf = symm.empty(self._FLAG_BYTES + 2 * slot_bytes, dtype=torch.uint8, device=device)
+        buf.zero_()
+        hdl = symm.rendezvous(buf, group)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        base = [int(x) for x in hdl.buffer_ptrs]
+        recv = [b + self._FLAG_BYTES for b in base]
+        state = torch.zeros(4, dtype=torch.int32, device=device)
+        self._p2p = (slot_bytes, buf, hdl, recv, base, state)
+        return self._p2p
+
+    def p2p_errors(self) -> int:
+        """Peer waits that gave up (state word 3) since the buffers were made."""
+        return 0 if self._p2p is None else int(self._p2p[5][3].item())
+
     def __call__(self, q_local, k_cache_local, v_cache_local, block_tables, seq_lens, scale=None, max_seq_len=None,
-                 out=None, workspace=None, gather: bool = False) -> torch.Tensor:
+                 out=None, workspace=None, gather: bool = False, gathered_out=None) -> torch.Tensor:
+        """This rank's heads ``[n, Hq/G, D]``, or with ``gather`` every head
+        ``[n, Hq, D]`` (into ``gathered_out`` when given)."""
         s = self.shard
         if q_local.shape[1] != s.q_per_rank or k_cache_local.shape[2] != s.kv_per_rank:
             raise ValueError(
@@ -139,7 +177,32 @@ class ShardedPagedAttention:
                                   max_seq_len=max_seq_len, out=out, workspace=workspace)
         if not gather or s.world == 1:
             return local
-        return gather_heads(local, s, self.group)
+        return self.gather(local, gathered_out)
+
+    def gather(self, local: torch.Tensor, gathered_out: torch.Tensor | None = None) -> torch.Tensor:
+        """Every rank's heads ``[n, Hq, D]`` from this rank's ``[n, Hq/G, D]``
+        (a collective: every rank calls it with the same sizes)."""
+        s = self.shard
+        if s.world == 1:
+            if gathered_out is None:
+                return local
+            gathered_out.copy_(local)
+            return gathered_out
+        if self.exchange == "p2p":
+            from . import capi
+
+            n, hpr, d = local.shape
+            if gathered_out is None:
+                gathered_out = torch.empty(n, s.num_q_heads, d, dtype=local.dtype, device=local.device)
+            _, _, _, recv, flags, state = self._p2p_buffers(n * s.num_q_heads * d * local.element_size(),
+                                                            local.device)
+            capi.gather_heads(local, recv, flags, state, gathered_out, s.rank, s.world, self.wait_limit_ms)
+            return gathered_out
+        full = gather_heads(local, s, self.group)
+        if gathered_out is not None:
+            gathered_out.copy_(full)
+            return gathered_out
+        return full
 
 
 

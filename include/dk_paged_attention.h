@@ -247,6 +247,40 @@ typedef struct DkPeerExchangeArgs {
 DK_API int dk_exchange_merge_lse(const DkPeerExchangeArgs* args, dk_stream_t stream);
 
 /*
+ * All-gather of KV-head shards over NVLink peer memory, one kernel per GPU:
+ * the alternative to an NCCL all-gather of the per-rank outputs (the gather
+ * a KV-head-sharded decode needs where its consumer wants every head).  Rank
+ * r holds query heads [r * heads_per_rank, (r + 1) * heads_per_rank) in
+ * `local` [num_seqs, heads_per_rank, head_dim]; every GPU of the group calls
+ * it once per step with the same sizes, and gets all num_q_heads =
+ * world * heads_per_rank heads in out [num_seqs, num_q_heads, head_dim].
+ * Memory as for dk_exchange_merge_lse:
+ *   recv[r]   [2][num_seqs * num_q_heads * head_dim] elements of `dtype` on GPU r
+ *   flags[r]  uint32 [world] on GPU r, zero before the first call
+ *   state     uint32 [4] on this GPU, zero before the first call
+ * (flags and state must not be shared with dk_exchange_merge_lse calls.)  The
+ * call stores `local` into slot (call parity) of every GPU's receive buffer,
+ * publishes its flag on every GPU, waits (bounded by wait_limit_ms; a
+ * give-up adds 1 to state[3] and the call goes on) for every rank's flag and
+ * copies the slot into `out`.  `local` and `out` rows must start on 16-byte
+ * boundaries (strides multiples of 8 elements).  world <= DK_MAX_PEERS.
+ */
+typedef struct DkPeerGatherArgs {
+  const void* local;               /* this GPU's heads [num_seqs, heads_per_rank, head_dim] of `dtype` */
+  int64_t local_stride_seq, local_stride_head;
+  void* recv[DK_MAX_PEERS];        /* receive buffers of ranks 0..world-1 as this GPU addresses them */
+  uint32_t* flags[DK_MAX_PEERS];   /* flag words of ranks 0..world-1 as this GPU addresses them */
+  uint32_t* state;
+  void* out;                       /* [num_seqs, world * heads_per_rank, head_dim] of `dtype` */
+  int64_t out_stride_seq, out_stride_head;
+  int32_t rank, world, num_seqs, heads_per_rank, head_dim;
+  int32_t dtype;                   /* DK_DTYPE_FLOAT16 / DK_DTYPE_BFLOAT16 */
+  uint32_t wait_limit_ms;          /* 0: 2000 */
+} DkPeerGatherArgs;
+
+DK_API int dk_gather_heads(const DkPeerGatherArgs* args, dk_stream_t stream);
+
+/*
  * Paged-KV write, the step before decode: no counterpart in DecodeKernels
  * (its decode reads caches that vLLM's reshape_and_cache_flash wrote); this
  * is that operation.  For every token t with slot = slot_mapping[t] in

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (dk_\w+)", out))
     assert set(_declared()) <= exported
-    assert capi.version() == 600
+    assert capi.version() == 700
 
 
 def test_struct_layout_matches_header(tmp_path):
@@ -44,7 +44,7 @@ def test_struct_layout_matches_header(tmp_path):
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dk_paged_attention.h"', "int main(void) {"]
     structs = (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan),
                ("DkCacheWriteArgs", capi.DkCacheWriteArgs), ("DkLseMergeArgs", capi.DkLseMergeArgs),
-               ("DkPeerExchangeArgs", capi.DkPeerExchangeArgs))
+               ("DkPeerExchangeArgs", capi.DkPeerExchangeArgs), ("DkPeerGatherArgs", capi.DkPeerGatherArgs))
     for struct, cls in structs:
         lines.append(f'  printf("{struct} sizeof %zu\\n", sizeof({struct}));')
         for name, _ in cls._fields_:

@@ -89,3 +89,121 @@ def test_two_nccl_ranks_gather():
                        capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("ok") == 2
+
+
+def test_peer_gather_world_one_copies_local_heads():
+    """dk_gather_heads with a group of one: the local heads land in out
+    (through the receive slot), call after call, with any out strides."""
+    from decodekernels_b200 import capi
+
+    n, hq, d = 5, 16, 128
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")
+    buf = torch.zeros(256 + 2 * n * hq * d * 2, dtype=torch.uint8, device="cuda")
+    for it in range(3):
+        local = torch.randn(n, hq, d, device="cuda").to(torch.bfloat16)
+        wide = torch.full((n, hq + 3, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        out = wide[:, 1:hq + 1]  # strided destination
+        capi.gather_heads(local, [buf.data_ptr() + 256], [buf.data_ptr()], state, out, rank=0, world=1)
+        torch.cuda.synchronize()
+        assert torch.equal(out, local)
+        assert int(state[0].item()) == it + 1 and int(state[3].item()) == 0
+
+
+def test_peer_gather_wait_gives_up_and_reports():
+    """One GPU, world 2: the second rank's flag is a word nothing sets, so the
+    gather's bounded wait runs out, records the give-up in state[3] and
+    returns; this rank's heads are in place and the context stays usable."""
+    from decodekernels_b200 import capi
+
+    n, hpr, d = 3, 4, 64
+    slot = n * 2 * hpr * d * 2
+    mine = torch.zeros(256 + 2 * slot, dtype=torch.uint8, device="cuda")
+    other = torch.zeros_like(mine)  # stands in for a peer that never calls
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")
+    local = torch.randn(n, hpr, d, device="cuda").to(torch.float16)
+    out = torch.zeros(n, 2 * hpr, d, dtype=torch.float16, device="cuda")
+    capi.gather_heads(local, [mine.data_ptr() + 256, other.data_ptr() + 256], [mine.data_ptr(), other.data_ptr()],
+                      state, out, rank=0, world=2, wait_limit_ms=100)
+    torch.cuda.synchronize()
+    assert int(state[3].item()) >= 1  # gave up instead of hanging
+    assert torch.equal(out[:, :hpr], local)
+    other_flags = other[:8].view(torch.int32)
+    assert int(other_flags[0].item()) == 1 and int(other_flags[1].item()) == 0  # we signalled; the peer never did
+    kv = make_paged_kv([100], 1, 128, 16, torch.bfloat16, "cuda")
+    q = torch.randn(1, 8, 128, device="cuda").to(torch.bfloat16)
+    assert_attention_close(dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens),
+                           oracle_dense(q, kv), torch.bfloat16, "after a given-up gather")
+
+
+_P2P_GATHER_SCRIPT = textwrap.dedent(
+    """
+    import datetime, os, sys
+    sys.path.insert(0, {root!r}); sys.path.insert(0, {tests!r})
+    import torch, torch.distributed as dist
+    from decodekernels_b200.sharded import ShardedPagedAttention, shard_cache, shard_queries
+    from decodekernels_b200.testing import make_paged_kv
+    from gpu_helpers import assert_attention_close, oracle_dense
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    L = 3000
+    lens0 = [7, 900, L, 64, 0, 1500, 513]
+    full = make_paged_kv([L] * len(lens0), 8, 128, 16, torch.float16, "cpu", layout="vllm", seed=41)
+    q_cpu = torch.randn(len(lens0), 32, 128, generator=torch.Generator().manual_seed(42), dtype=torch.float16)
+    p2p = ShardedPagedAttention(32, 8, exchange="p2p")
+    nccl = ShardedPagedAttention(32, 8)
+    s = p2p.shard
+    k, v = shard_cache(full.k_cache, s).cuda(), shard_cache(full.v_cache, s).cuda()  # this rank's heads only
+    q = shard_queries(q_cpu, s).contiguous().cuda()
+    bt = full.block_tables.cuda()
+    lens = torch.tensor(lens0, dtype=torch.int32, device="cuda")
+    out = torch.empty(len(lens0), 32, 128, dtype=torch.float16, device="cuda")
+
+    def step():
+        p2p(q, k, v, bt, lens, max_seq_len=L, gather=True, gathered_out=out)
+
+    g = torch.Generator().manual_seed(43)
+    for it in range(4):  # eager calls: the device-side call counter advances in lockstep
+        lens.copy_(torch.randint(0, L + 1, (len(lens0),), generator=g, dtype=torch.int32))
+        step()
+        torch.cuda.synchronize()
+        full.seq_lens.copy_(lens.cpu())
+        assert_attention_close(out, oracle_dense(q_cpu, full), torch.float16, "rank %d eager %d" % (rank, it))
+        ref = nccl(q, k, v, bt, lens, max_seq_len=L, gather=True)
+        assert torch.equal(ref, out), "p2p and NCCL gathers differ"
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        step()
+    torch.cuda.current_stream().wait_stream(st)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for it in range(3):
+        lens.copy_(torch.randint(0, L + 1, (len(lens0),), generator=g, dtype=torch.int32))
+        graph.replay()
+        torch.cuda.synchronize()
+        full.seq_lens.copy_(lens.cpu())
+        assert_attention_close(out, oracle_dense(q_cpu, full), torch.float16, "rank %d graph %d" % (rank, it))
+    del graph
+    assert p2p.p2p_errors() == 0
+    dist.barrier()
+    dist.destroy_process_group()
+    print("rank", rank, "ok")
+    """
+)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_peer_memory_gather():
+    script = _P2P_GATHER_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
+    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    f = os.path.join(path, "head_sharded_p2p_case.py")
+    with open(f, "w") as fh:
+        fh.write(script)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29541", f],
+                       capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert r.stdout.count("ok") == 2
