@@ -274,6 +274,10 @@ constexpr int kCompactMinPartitions = DK_COMPACT_MIN_PARTITIONS;
 constexpr int kCompactWaves = DK_COMPACT_WAVES;
 constexpr long long kFusedMergeMaxBytes = DK_FUSED_MERGE_MAX_BYTES;
 constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
+#ifndef DK_PLAN_VARIED_WAVES
+#define DK_PLAN_VARIED_WAVES 8
+#endif
+constexpr int kVariedWaves = DK_PLAN_VARIED_WAVES;
 constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
 
 int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms, int kv_bytes = 2) {
@@ -283,10 +287,19 @@ int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max
   const long long token_bytes = 2LL * kv_bytes * head_dim;  // K + V
   int ps = round_up((work + slots - 1) / slots, DK_TILE_TOKENS);
   long long cap = kMaxBytes / token_bytes;
-  // The balance cap for varying lengths is in 16-bit tokens whatever the
-  // cache: an e4m3 CTA's time follows its tokens (its math is the limit), and
-  // e4m3 c2 measured 6% faster at 1024 tokens than at 2048.
-  if (num_seqs > 1 && pairs < 4 * slots) cap = std::min(cap, kVariedBytes / (4LL * head_dim));
+  // Varying lengths balance over many CTAs: with few (sequence, KV head)
+  // pairs, about kVariedWaves waves of CTAs if every sequence had
+  // max_seq_len tokens, within [kVariedBytes, kMaxBytes].  In 16-bit tokens
+  // whatever the cache: an e4m3 CTA's time follows its tokens (its math is
+  // the limit), and e4m3 c2 measured 6% faster at 1024 tokens than at 2048.
+  // (8 waves, against the former fixed kVariedBytes cap: a rank's share of c5
+  // at 2 / 4 / 8 GPUs 1188 -> 1153, 601 -> 589, 310 -> 303 us; of e4m3 c5 at
+  // 2 / 8 GPUs 672 -> 620, 190 -> 178 us; c4 85.3 -> 83.4, e4m3 c4 68.3 ->
+  // 62.4 us; c2 unchanged.  16 waves was slower on c4.)
+  if (num_seqs > 1 && pairs < 4 * slots) {
+    const long long want = work / (static_cast<long long>(kVariedWaves) * slots);
+    cap = std::min(cap, std::max(kVariedBytes / (4LL * head_dim), std::min(kMaxBytes / (4LL * head_dim), want)));
+  }
   cap = std::max<long long>(DK_TILE_TOKENS, cap / DK_TILE_TOKENS * DK_TILE_TOKENS);
   return static_cast<int>(std::min<long long>(std::max(ps, kMinPartition), cap));
 }
