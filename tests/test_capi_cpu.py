@@ -226,3 +226,30 @@ def test_empty_batch_is_a_no_op():
     rc, p = _plan(a)
     assert rc == 0 and p["path"] == capi.DK_PATH_NONE
     assert capi.load().dk_paged_attention_decode(ctypes.byref(a), None) == 0
+
+
+def _wide_ws(n, hq, parts, d):
+    """A workspace's shape without its memory (the planner reads sizes only)."""
+    z = torch.zeros(1)
+    return (z.expand(n, hq, parts, d), z.expand(n, hq, parts), z.expand(n, hq, parts))
+
+
+@pytest.mark.parametrize(
+    "n,hq,hkv,d,bs,L,want",
+    [
+        (256, 64, 8, 128, 16, 32768, 4096),  # c5: many (sequence, KV head) pairs -> the byte cap
+        (256, 32, 4, 128, 16, 32768, 4096),  # a rank's share of c5 at 2 GPUs (1024 pairs)
+        (256, 16, 2, 128, 16, 32768, 4096),  # ... at 4 GPUs
+        (256, 8, 1, 128, 16, 32768, 3520),   # ... at 8 GPUs: ~8 waves of CTAs at max_seq_len
+        (64, 32, 8, 128, 16, 4096, 1024),    # c2: the 512 KB floor
+        (128, 8, 1, 256, 32, 32768, 1728),   # c4 (MQA, D = 256)
+    ],
+)
+def test_planner_partition_sizes(n, hq, hkv, d, bs, L, want):
+    """The planner's choices for the measured shapes (148 SMs assumed without
+    a GPU): few pairs get partitions for ~8 waves of CTAs, within
+    [512 KB, 2 MB] of 16-bit K+V."""
+    rc, p = _plan(_args(n=n, hq=hq, hkv=hkv, d=d, bs=bs, max_seq_len=L, ws=_wide_ws(n, hq, -(-L // 64), d)))
+    assert rc == 0, capi.last_error()
+    assert p["partition_size"] == want
+    assert p["num_partitions"] == -(-L // want)

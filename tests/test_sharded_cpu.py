@@ -104,3 +104,15 @@ def test_dead_rank_fails_the_collective_instead_of_hanging():
     outdir = _run("dead")
     err = os.path.join(outdir, "rank0.err")
     assert os.path.exists(err), "rank 0 finished a gather whose peer had exited"
+
+
+def test_head_sharded_exchange_must_be_known():
+    from decodekernels_b200.sharded import ShardedPagedAttention
+
+    with pytest.raises(ValueError, match="exchange"):
+        ShardedPagedAttention(32, 8, rank=0, world=1, exchange="mpi")
+    attn = ShardedPagedAttention(32, 8, rank=0, world=1, exchange="p2p")
+    local = torch.randn(3, 32, 64)
+    assert attn.gather(local) is local  # a group of one needs no exchange
+    dst = torch.empty_like(local)
+    assert attn.gather(local, dst) is dst and torch.equal(dst, local)
