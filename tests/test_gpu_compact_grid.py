@@ -101,3 +101,44 @@ def test_persistent_repeated_calls_identical():
         again, _ = _run(q, kv, 64, capi.DK_FLAG_PERSISTENT, False)
         assert torch.equal(again, first)
     assert capi.wait_timeouts(0) == 0
+
+
+@pytest.mark.parametrize("n", [512, 513])
+def test_compact_grid_at_its_sequence_limit(n):
+    """512 sequences: the warp scan's largest batch (16 lengths per lane); 513
+    falls back to the dense grid.  Both agree bit for bit with the dense grid
+    and match the oracle on a sample of sequences."""
+    g = torch.Generator().manual_seed(n)
+    lens = torch.randint(0, 1200, (n,), generator=g).tolist()
+    kv = make_paged_kv(lens, 1, 128, 16, torch.bfloat16, "cuda", layout="nhd", seed=n)
+    q = _q(n, 4, 128, torch.bfloat16, seed=n)
+    default, plan = _run(q, kv, 64, 0, False)
+    persistent, _ = _run(q, kv, 64, capi.DK_FLAG_PERSISTENT, False)
+    assert torch.equal(persistent, default)
+    want = oracle_dense(q[:64], type(kv)(kv.k_cache, kv.v_cache, kv.block_tables[:64], kv.seq_lens[:64],
+                                         kv.block_size))
+    assert_attention_close(default[:64], want, torch.bfloat16, f"n={n}")
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_persistent_lse_partials(fp8):
+    """The LSE-partials entry point (sequence sharding) on the persistent grid
+    writes the same rows as on the default grid."""
+    lens = _lens(24, seed=5, max_len=3000)
+    kv = make_paged_kv(lens, 2, 128, 16, torch.float16, "cuda", layout="hnd", seed=6)
+    q = _q(len(lens), 8, 128, torch.float16, seed=7)
+    k, v, ks, vs = kv.k_cache, kv.v_cache, 1.0, 1.0
+    if fp8:
+        k, v = fp8_caches(kv, "hnd", KS, VS)
+        ks, vs = KS, VS
+    n, hq, d = q.shape
+    L = max(lens)
+    rows = []
+    for flags in (0, capi.DK_FLAG_PERSISTENT):
+        part = torch.full((n, hq, d + 4), float("nan"), device="cuda")
+        ws = tuple(torch.empty(s, device="cuda") for s in ((n, hq, 64, d), (n, hq, 64), (n, hq, 64)))
+        capi.decode_lse(q, k, v, kv.block_tables, kv.seq_lens, d**-0.5, L, part, ws, 64, flags=flags, k_scale=ks,
+                        v_scale=vs)
+        torch.cuda.synchronize()
+        rows.append(part)
+    assert torch.equal(rows[0][..., :d + 1], rows[1][..., :d + 1])
