@@ -380,12 +380,12 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   // Merge counters turn the merge into the last partition's epilogue, which
   // saves the merge kernel's launch and latency but costs every partition a
   // release + atomic round trip and leaves each pair's merge to one CTA.
-  // Measured worth it for a grid of about one wave whose pairs have a few KB
-  // of rows (c1: 13.3 -> 12.x us); multi-wave grids (c2) and large merges
-  // (c3, c4) are faster with the separate kernel.
+  // Measured worth it when each pair's rows are small (c1 13.3 -> 12.x us,
+  // c2 105.7 -> 103-105, c5 and a rank's share of c5 at 2 / 4 / 8 GPUs
+  // 0.2-0.4% faster); large merges are faster with the separate kernel
+  // (c3 86 vs 90.5 us, c4 83 vs 90 us).
   const long long merge_bytes = 1LL * parts * (a.num_q_heads / a.num_kv_heads) * (a.head_dim + 2) * 4;
-  const long long one_wave = static_cast<long long>(kPlanCtasPerSm) * num_sms(dev);
-  const bool small = merge_bytes <= kFusedMergeMaxBytes && pl->num_ctas <= one_wave;
+  const bool small = merge_bytes <= kFusedMergeMaxBytes;
   const bool fused = pl->split && a.merge_counters != nullptr && (small || (a.flags & DK_FLAG_FORCE_FUSED_MERGE));
   pl->launches = pl->split && !fused ? 2 : 1;
 }
