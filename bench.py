@@ -352,8 +352,10 @@ def run_gpu_arm(args) -> None:
         sampler.stop()
 
     # With N GPUs, also time the variant whose consumer needs every head on
-    # every rank: decode + all-gather of the per-head outputs (our NVLink
-    # peer-memory kernel, or NCCL with --exchange nccl).
+    # every rank: decode + all-gather of the per-head outputs -- with
+    # --exchange p2p the gather rides on the decode's output stores (peer
+    # stores over NVLink, dk_paged_attention_decode_gather), with nccl an
+    # all_gather_into_tensor follows the decode.
     gather_s = None
     gatherer = None
     if world > 1 and not seq_mode:
@@ -362,15 +364,26 @@ def run_gpu_arm(args) -> None:
         gatherer = ShardedPagedAttention(batch.config.num_q_heads, batch.config.num_kv_heads, rank, world,
                                          exchange=args.exchange)
         full_out = torch.empty(out.shape[0], batch.config.num_q_heads, out.shape[2], dtype=out.dtype, device=dev)
+
+        def gather_step():
+            if args.exchange == "p2p" and not batch.config.kv_fp8:
+                gatherer(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=max_len,
+                         workspace=ws, gather=True, gathered_out=full_out)
+            else:
+                step()
+                gatherer.gather(out, full_out)
+
         for _ in range(3):
-            gatherer.gather(out, full_out)
+            gather_step()
+        torch.cuda.synchronize()
+        if not torch.equal(full_out[:, rank * out.shape[1]:(rank + 1) * out.shape[1]], out):
+            raise SystemExit(f"rank {rank}: the gathered output's own heads differ from the decode's")
         torch.distributed.barrier()
         torch.cuda.synchronize()
         gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         gs.record(stream)
         for _ in range(args.steps):
-            step()
-            gatherer.gather(out, full_out)
+            gather_step()
         ge.record(stream)
         torch.cuda.synchronize()
         gather_s = gs.elapsed_time(ge) * 1e-3
@@ -540,7 +553,9 @@ def run_gpu_arm(args) -> None:
             "with_gather": None if not gather_s else {
                 "us_per_call": gather_s / args.steps * 1e6, "value": kv_total / (gather_s / args.steps) / 1e12,
                 "unit": UNIT, "note": "decode + all-gather of the per-head outputs to every rank ("
-                + ("one NVLink peer-memory kernel, dk_gather_heads)" if args.exchange == "p2p" else "NCCL)")},
+                + ("NCCL)" if args.exchange != "p2p" else
+                   "one NVLink peer-memory kernel after the decode, dk_gather_heads)" if batch.config.kv_fp8 else
+                   "fused into the decode's output stores over NVLink peer memory, dk_paged_attention_decode_gather)")},
             "clocks": sampler.summary(t0, t1) if sampler else None,
             "wall_s_timed": t1 - t0,
         }

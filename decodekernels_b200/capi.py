@@ -33,7 +33,8 @@ DK_NOALLOC_SCRATCH_BYTES = 32 * 1024 * 1024
 
 EXPORTED = ("dk_paged_attention_decode", "dk_plan", "dk_num_partitions", "dk_last_error",
             "dk_device_wait_timeouts", "dk_version", "dk_paged_attention_decode_noalloc", "dk_reshape_and_cache",
-            "dk_paged_attention_decode_lse", "dk_merge_lse", "dk_exchange_merge_lse", "dk_gather_heads")
+            "dk_paged_attention_decode_lse", "dk_merge_lse", "dk_exchange_merge_lse", "dk_gather_heads",
+            "dk_paged_attention_decode_gather")
 
 
 class DkPagedAttnArgs(ctypes.Structure):
@@ -220,6 +221,9 @@ def load() -> ctypes.CDLL:
         lib.dk_exchange_merge_lse.restype = ctypes.c_int
         lib.dk_gather_heads.argtypes = [ctypes.POINTER(DkPeerGatherArgs), ctypes.c_void_p]
         lib.dk_gather_heads.restype = ctypes.c_int
+        lib.dk_paged_attention_decode_gather.argtypes = [ctypes.POINTER(DkPagedAttnArgs),
+                                                         ctypes.POINTER(DkPeerGatherArgs), ctypes.c_void_p]
+        lib.dk_paged_attention_decode_gather.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -452,6 +456,35 @@ def gather_heads(local, recv_ptrs, flag_ptrs, state, out, rank: int, world: int,
     rc = load().dk_gather_heads(ctypes.byref(a), ctypes.c_void_p(stream))
     if rc != 0:
         raise RuntimeError(f"dk_gather_heads failed ({rc}): {last_error()}")
+    return rc
+
+
+def decode_gather(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, workspace, recv_ptrs, flag_ptrs,
+                  state, out, rank: int, world: int, wait_limit_ms: int = 0, flags: int = 0, k_scale: float = 1.0,
+                  v_scale: float = 1.0, stream=None) -> int:
+    """dk_paged_attention_decode_gather: decode this rank's heads ``q``
+    [n, Hq / world, D] with the output rows stored straight into every
+    rank's receive slot, then all heads into ``out`` [n, Hq, D]."""
+    import torch
+
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, workspace, 0, False, flags,
+                  k_scale, v_scale)
+    g = DkPeerGatherArgs()
+    g.local = 0
+    for r in range(world):
+        g.recv[r] = recv_ptrs[r]
+        g.flags[r] = flag_ptrs[r]
+    g.state = state.data_ptr()
+    g.out, g.out_stride_seq, g.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    g.rank, g.world = rank, world
+    g.num_seqs, g.heads_per_rank, g.head_dim = q.shape[0], q.shape[1], q.shape[2]
+    g.dtype = _dtype_code(out)
+    g.wait_limit_ms = wait_limit_ms
+    if stream is None:
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = load().dk_paged_attention_decode_gather(ctypes.byref(a), ctypes.byref(g), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"dk_paged_attention_decode_gather failed ({rc}): {last_error()}")
     return rc
 
 

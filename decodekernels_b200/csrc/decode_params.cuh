@@ -10,6 +10,7 @@ constexpr int kSubTokens = 16;       // tokens per consumer warp per tile (mma M
 constexpr int kSimtThreads = 128;
 constexpr int kMergeThreads = 256;
 constexpr int kMaxGroup = 8;         // query heads per KV head (mma N)
+constexpr int kMaxPeers = 8;         // GPUs of a peer-memory group (DK_MAX_PEERS)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -52,6 +53,17 @@ struct DecodeParams {
   int kv_fp8;          // 1: the caches hold e4m3 bytes
   int compact;         // 1: live work items numbered densely (compact_coords); CTA b runs items b, b + G, ...
   int persistent;      // 1 (with compact): the grid is one wave of resident CTAs
+  // Head all-gather fused into the output stores (dk_paged_attention_decode_gather):
+  // with peer_world > 0 every output row goes, instead of to `out`, to slot
+  // (call parity) of every rank's receive buffer [2][num_seqs, peer_q_heads, D]
+  // at head peer_head0 + q_head; the parity is that of peer_state[0] + 1 (the
+  // gathers completed so far + 1, read on the device).
+  void* peer_recv[kMaxPeers];
+  const uint32_t* peer_state;
+  int64_t peer_slot_elems;  // num_seqs * peer_q_heads * D
+  int peer_world;
+  int peer_head0;
+  int peer_q_heads;
 };
 
 // (partition, kv_head, seq) of this CTA in the 1-D grid, sequence-major:

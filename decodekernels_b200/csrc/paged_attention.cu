@@ -663,7 +663,13 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
   return 0;
 }
 
-int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream, bool lse_mode = false) {
+// Receive slots of a head all-gather fused into the decode's output stores.
+struct PeerOutputs {
+  const DkPeerGatherArgs* g;
+};
+
+int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t stream, bool lse_mode = false,
+           const PeerOutputs* peer = nullptr) {
   if (1LL * pl.num_partitions * a.num_kv_heads * a.num_seqs > INT_MAX)
     return fail(1, "paged_attention_decode: %d partitions x %d KV heads x %d sequences exceed one grid", pl.num_partitions,
                 a.num_kv_heads, a.num_seqs);
@@ -720,6 +726,15 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.persistent = p.compact && persistent;
   p.scale_log2 = a.scale * (a.kv_fp8 ? a.k_scale : 1.0f) * kLog2e;
   p.v_scale = a.kv_fp8 ? a.v_scale : 1.0f;
+  if (peer != nullptr) {
+    const DkPeerGatherArgs& g = *peer->g;
+    for (int r = 0; r < g.world; ++r) p.peer_recv[r] = g.recv[r];
+    p.peer_state = g.state;
+    p.peer_world = g.world;
+    p.peer_q_heads = g.heads_per_rank * g.world;
+    p.peer_head0 = g.rank * g.heads_per_rank;
+    p.peer_slot_elems = static_cast<int64_t>(g.num_seqs) * p.peer_q_heads * g.head_dim;
+  }
   const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;
   switch (a.head_dim) {
     case 64:
@@ -866,7 +881,7 @@ int launch_peer_exchange(const DkPeerExchangeArgs& a, int dev, cudaStream_t stre
   return e == cudaSuccess ? 0 : fail_cuda(e, "peer exchange kernel launch");
 }
 
-int validate_peer_gather(const DkPeerGatherArgs* a) {
+int validate_peer_gather(const DkPeerGatherArgs* a, bool need_local = true) {
   if (a == nullptr) return fail(1, "dk_gather_heads: args is NULL");
   if (a->world < 1 || a->world > DK_MAX_PEERS || a->rank < 0 || a->rank >= a->world)
     return fail(1, "dk_gather_heads: need 0 <= rank < world <= %d", DK_MAX_PEERS);
@@ -875,9 +890,11 @@ int validate_peer_gather(const DkPeerGatherArgs* a) {
   if (a->dtype != DK_DTYPE_FLOAT16 && a->dtype != DK_DTYPE_BFLOAT16)
     return fail(1, "dk_gather_heads: dtype must be float16 or bfloat16 (code %d)", a->dtype);
   if (a->num_seqs < 0 || a->heads_per_rank <= 0) return fail(1, "dk_gather_heads: bad sizes");
-  if (!a->local || !a->state || !a->out) return fail(1, "dk_gather_heads: NULL pointer");
-  if (!aligned(a->local, 16) || !aligned(a->out, 16) || a->local_stride_seq % 8 || a->local_stride_head % 8 ||
-      a->out_stride_seq % 8 || a->out_stride_head % 8)
+  const bool rows = a->num_seqs > 0;  // with no rows only the flags move (local and out may be NULL)
+  if ((rows && need_local && !a->local) || !a->state || (rows && !a->out))
+    return fail(1, "dk_gather_heads: NULL pointer");
+  if ((rows && need_local && (!aligned(a->local, 16) || a->local_stride_seq % 8 || a->local_stride_head % 8)) ||
+      !aligned(a->out, 16) || a->out_stride_seq % 8 || a->out_stride_head % 8)
     return fail(1, "dk_gather_heads: local and out rows must start on 16-byte boundaries");
   for (int r = 0; r < a->world; ++r) {
     if (!a->recv[r] || !a->flags[r]) return fail(1, "dk_gather_heads: NULL peer pointer for rank %d", r);
@@ -887,10 +904,10 @@ int validate_peer_gather(const DkPeerGatherArgs* a) {
   return 0;
 }
 
-int launch_peer_gather(const DkPeerGatherArgs& a, int dev, cudaStream_t stream) {
+int launch_peer_gather(const DkPeerGatherArgs& a, int dev, cudaStream_t stream, bool push = true) {
   PeerGatherParams p;
   std::memset(&p, 0, sizeof(p));
-  p.local = static_cast<const uint16_t*>(a.local);
+  p.local = push ? static_cast<const uint16_t*>(a.local) : nullptr;  // nullptr: the decode already pushed
   p.local_stride_seq = a.local_stride_seq;
   p.local_stride_head = a.local_stride_head;
   for (int r = 0; r < a.world; ++r) {
@@ -1139,6 +1156,33 @@ int dk_exchange_merge_lse(const DkPeerExchangeArgs* args, dk_stream_t stream) {
     default:
       return dkb::launch_peer_exchange<256>(*args, dev, s);
   }
+}
+
+int dk_paged_attention_decode_gather(const DkPagedAttnArgs* args, const DkPeerGatherArgs* gather,
+                                     dk_stream_t stream) {
+  if (args == nullptr) return dkb::fail(1, "dk_paged_attention_decode_gather: args is NULL");
+  if (int e = dkb::validate_peer_gather(gather, false)) return e;
+  DkPagedAttnArgs a = *args;
+  if (gather->num_seqs != a.num_seqs || gather->heads_per_rank != a.num_q_heads || gather->head_dim != a.head_dim ||
+      gather->dtype != a.dtype)
+    return dkb::fail(1,
+                     "dk_paged_attention_decode_gather: the gather's num_seqs, heads_per_rank, head_dim and dtype must "
+                     "be the decode's num_seqs, num_q_heads, head_dim and dtype");
+  a.out = gather->out;  // validated as a place to write; the decode's rows go to the receive slots
+  a.out_stride_seq = gather->out_stride_seq;
+  a.out_stride_head = gather->out_stride_head;
+  if (int e = dkb::validate(&a)) return e;
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaGetDevice");
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (a.num_seqs > 0) {
+    DkPlan pl;
+    dkb::make_plan(a, dev, &pl);
+    const dkb::PeerOutputs peer{gather};
+    if (int e = dkb::launch(a, pl, dev, s, false, &peer)) return e;
+  }
+  return dkb::launch_peer_gather(*gather, dev, s, false);  // every rank publishes and waits, even with no rows
 }
 
 int dk_gather_heads(const DkPeerGatherArgs* args, dk_stream_t stream) {

@@ -20,6 +20,14 @@ namespace dkb {
 // is stored as a natural log by the thread that writes d == 0.
 template <typename T, int D>
 __device__ __forceinline__ void store_out4(const DecodeParams& p, int seq, int q_head, int d, float4 o, float lse2) {
+  if (p.peer_world > 0) {  // fused head all-gather: this rank's heads into every rank's receive slot
+    // the previous call's gather kernel wrote it: read through L2, after the grid-dependency wait
+    const int64_t slot = static_cast<int64_t>((__ldcg(p.peer_state) + 1u) & 1u) * p.peer_slot_elems;
+    const int64_t at = slot + (static_cast<int64_t>(seq) * p.peer_q_heads + p.peer_head0 + q_head) * D + d;
+    const uint2 v = make_uint2(Conv<T>::pack2(o.x, o.y), Conv<T>::pack2(o.z, o.w));
+    for (int r = 0; r < p.peer_world; ++r) *reinterpret_cast<uint2*>(static_cast<T*>(p.peer_recv[r]) + at) = v;
+    return;
+  }
   if (p.lse_mode) {
     float* row = static_cast<float*>(p.out) + seq * p.out_stride_seq + q_head * p.out_stride_head;
     *reinterpret_cast<float4*>(row + d) = o;

@@ -28,7 +28,6 @@
 
 namespace dkb {
 
-constexpr int kMaxPeers = 8;
 constexpr int kExchangeThreads = 256;
 
 struct PeerExchangeParams {
@@ -192,8 +191,9 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_gather_kernel(const Pee
   const int chunks = p.head_dim >> 3;  // 16-byte chunks per row
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kExchangeThreads;
 
-  // 1. push this rank's rows into slot (e % 2) of every rank
-  const int64_t mine = static_cast<int64_t>(p.num_seqs) * p.heads_per_rank * chunks;
+  // 1. push this rank's rows into slot (e % 2) of every rank (none when the
+  //    decode's output stores already did: local == nullptr)
+  const int64_t mine = p.local == nullptr ? 0 : static_cast<int64_t>(p.num_seqs) * p.heads_per_rank * chunks;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExchangeThreads + tid; i < mine; i += stride) {
     const int64_t row = i / chunks;
     const int c = static_cast<int>(i - row * chunks);

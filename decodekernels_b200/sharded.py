@@ -132,6 +132,7 @@ class ShardedPagedAttention:
         self.exchange = exchange
         self.wait_limit_ms = wait_limit_ms
         self._p2p = None
+        self._native = attention_fn is None  # the sm_100a kernels: the gather can ride on the decode's stores
         if attention_fn is None:
             from .ops import paged_attention_decode
 
@@ -173,11 +174,36 @@ class ShardedPagedAttention:
                 f"{q_local.shape[1]} and {k_cache_local.shape[2]}")
         if scale is None:
             scale = q_local.shape[-1] ** -0.5  # the full model's scale, not a per-shard one
+        if gather and s.world > 1 and self.exchange == "p2p" and self._native:
+            return self._decode_gather(q_local, k_cache_local, v_cache_local, block_tables, seq_lens, scale,
+                                       max_seq_len, workspace, gathered_out)
         local = self.attention_fn(q_local, k_cache_local, v_cache_local, block_tables, seq_lens, scale=scale,
                                   max_seq_len=max_seq_len, out=out, workspace=workspace)
         if not gather or s.world == 1:
             return local
         return self.gather(local, gathered_out)
+
+    def _decode_gather(self, q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, workspace,
+                       gathered_out):
+        """Decode with the all-gather fused into the output stores
+        (``dk_paged_attention_decode_gather``): every rank's rows go straight
+        into every rank's receive slot; one small kernel then waits and copies."""
+        from . import capi
+        from .ops import alloc_workspace
+
+        s = self.shard
+        n, hpr, d = q.shape
+        if max_seq_len is None:
+            max_seq_len = int(seq_lens[:n].max().item()) if n > 0 else 0
+        if gathered_out is None:
+            gathered_out = torch.empty(n, s.num_q_heads, d, dtype=q.dtype, device=q.device)
+        if workspace is None:
+            workspace = alloc_workspace(n, hpr, d, max_seq_len, q.device, num_kv_heads=k_cache.shape[2],
+                                        block_size=k_cache.shape[1], merge_counters=True)
+        _, _, _, recv, flags, state = self._p2p_buffers(n * s.num_q_heads * d * q.element_size(), q.device)
+        capi.decode_gather(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, workspace, recv, flags,
+                           state, gathered_out, s.rank, s.world, self.wait_limit_ms)
+        return gathered_out
 
     def gather(self, local: torch.Tensor, gathered_out: torch.Tensor | None = None) -> torch.Tensor:
         """Every rank's heads ``[n, Hq, D]`` from this rank's ``[n, Hq/G, D]``

@@ -281,6 +281,22 @@ typedef struct DkPeerGatherArgs {
 DK_API int dk_gather_heads(const DkPeerGatherArgs* args, dk_stream_t stream);
 
 /*
+ * Decode + head all-gather with the gather fused into the decode: the
+ * kernels that write the output rows (partition epilogue, single-launch
+ * merge or merge kernel) store them straight into slot (call parity) of
+ * every rank's receive buffer over NVLink, and one small kernel then
+ * publishes this rank's flag, waits for every rank's and copies the slot into
+ * gather->out.  `args` is a decode of this rank's heads (args->out and its
+ * strides are not used; gather->out receives all world * num_q_heads heads);
+ * `gather` is as for dk_gather_heads with `local` unused (may be NULL), and
+ * its num_seqs / heads_per_rank / head_dim / dtype must equal the decode's
+ * num_seqs / num_q_heads / head_dim / dtype.  Every rank of the group calls
+ * it once per step (also with num_seqs == 0).  Not with lse output.
+ */
+DK_API int dk_paged_attention_decode_gather(const DkPagedAttnArgs* args, const DkPeerGatherArgs* gather,
+                                            dk_stream_t stream);
+
+/*
  * Paged-KV write, the step before decode: no counterpart in DecodeKernels
  * (its decode reads caches that vLLM's reshape_and_cache_flash wrote); this
  * is that operation.  For every token t with slot = slot_mapping[t] in

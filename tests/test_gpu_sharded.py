@@ -109,6 +109,39 @@ def test_peer_gather_world_one_copies_local_heads():
         assert int(state[0].item()) == it + 1 and int(state[3].item()) == 0
 
 
+@pytest.mark.parametrize("counters", [False, True])
+def test_fused_decode_gather_world_one_equals_decode(counters):
+    """dk_paged_attention_decode_gather with a group of one: the decode's
+    output stores go to the receive slot, the small kernel copies them to out;
+    bit-identical to the plain decode, call after call (both slot parities),
+    with the merge kernel or the single-launch merge, and with no sequences."""
+    from decodekernels_b200 import capi
+
+    lens = [1, 513, 3000, 0, 1200, 64]
+    kv = make_paged_kv(lens, 2, 128, 16, torch.bfloat16, "cuda", layout="vllm", seed=3)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(len(lens), 16, 128, generator=g, device="cuda").to(torch.bfloat16)
+    n, hq, d = q.shape
+    ws = dk.alloc_workspace(n, hq, d, 3000, "cuda", num_kv_heads=2, block_size=16, merge_counters=counters)
+    want = dk.paged_attention_decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, max_seq_len=3000,
+                                     workspace=ws)
+    state = torch.zeros(4, dtype=torch.int32, device="cuda")
+    buf = torch.zeros(256 + 2 * n * hq * d * 2, dtype=torch.uint8, device="cuda")
+    for it in range(3):
+        wide = torch.full((n, hq + 2, d), float("nan"), dtype=torch.bfloat16, device="cuda")
+        out = wide[:, 2:]
+        capi.decode_gather(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, 3000, ws,
+                           [buf.data_ptr() + 256], [buf.data_ptr()], state, out, rank=0, world=1)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), f"call {it}"
+        assert int(state[0].item()) == it + 1 and int(state[3].item()) == 0
+    empty = torch.empty(0, hq, d, dtype=torch.bfloat16, device="cuda")
+    capi.decode_gather(q[:0], kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, 3000, ws,
+                       [buf.data_ptr() + 256], [buf.data_ptr()], state, empty, rank=0, world=1)
+    torch.cuda.synchronize()
+    assert int(state[0].item()) == 4  # the collective still ran
+
+
 def test_peer_gather_wait_gives_up_and_reports():
     """One GPU, world 2: the second rank's flag is a word nothing sets, so the
     gather's bounded wait runs out, records the give-up in state[3] and
@@ -170,7 +203,9 @@ _P2P_GATHER_SCRIPT = textwrap.dedent(
         full.seq_lens.copy_(lens.cpu())
         assert_attention_close(out, oracle_dense(q_cpu, full), torch.float16, "rank %d eager %d" % (rank, it))
         ref = nccl(q, k, v, bt, lens, max_seq_len=L, gather=True)
-        assert torch.equal(ref, out), "p2p and NCCL gathers differ"
+        assert torch.equal(ref, out), "fused p2p and NCCL gathers differ"
+        local = nccl(q, k, v, bt, lens, max_seq_len=L)
+        assert torch.equal(p2p.gather(local), out), "fused and unfused p2p gathers differ"
     st = torch.cuda.Stream()
     st.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(st):
@@ -196,6 +231,9 @@ _P2P_GATHER_SCRIPT = textwrap.dedent(
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_ranks_peer_memory_gather():
+    """Two GPUs: the gather fused into the decode's output stores equals the
+    separate peer-memory gather and NCCL's, and the oracle, eagerly and under
+    CUDA-graph replay."""
     script = _P2P_GATHER_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
     path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
     f = os.path.join(path, "head_sharded_p2p_case.py")
