@@ -73,17 +73,31 @@ def _register_fakes() -> None:
         return None
 
 
-try:
-    if not TORCH_LIB_PATH.exists():
-        raise ImportError(f"{TORCH_LIB_PATH} is not built")
-    torch.ops.load_library(str(TORCH_LIB_PATH))  # registers torch.ops.decode_kernels.paged_attention_decode{,_fused}
-    capi.load()
-    _register_fakes()
-    _AVAILABLE = True
-    _IMPORT_ERROR: Exception | None = None
-except Exception as e:  # native library missing or stale: every op raises, nothing falls back
-    _AVAILABLE = False
-    _IMPORT_ERROR = e
+_AVAILABLE = False
+_IMPORT_ERROR: Exception | None = None
+
+
+def load_native() -> bool:
+    """Load both native libraries (at import, and again after a build in
+    the same process); True when they are loaded.  A missing or stale library
+    leaves every op raising -- nothing falls back."""
+    global _AVAILABLE, _IMPORT_ERROR
+    if _AVAILABLE:
+        return True
+    try:
+        if not TORCH_LIB_PATH.exists():
+            raise ImportError(f"{TORCH_LIB_PATH} is not built")
+        torch.ops.load_library(str(TORCH_LIB_PATH))  # registers torch.ops.decode_kernels.*
+        capi._lib = None  # a failed earlier load must not stick
+        capi.load()
+        _register_fakes()
+        _AVAILABLE, _IMPORT_ERROR = True, None
+    except Exception as e:
+        _AVAILABLE, _IMPORT_ERROR = False, e
+    return _AVAILABLE
+
+
+load_native()
 
 
 def is_available() -> bool:
