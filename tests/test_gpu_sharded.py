@@ -191,9 +191,13 @@ _P2P_GATHER_SCRIPT = textwrap.dedent(
     bt = full.block_tables.cuda()
     lens = torch.tensor(lens0, dtype=torch.int32, device="cuda")
     out = torch.empty(len(lens0), 32, 128, dtype=torch.float16, device="cuda")
+    # one workspace kind for every path (merge counters: the single-launch
+    # merge), so their plans match and the outputs can be compared bit for bit
+    import decodekernels_b200 as dk
+    ws = dk.alloc_workspace(len(lens0), 16, 128, L, "cuda", num_kv_heads=4, block_size=16, merge_counters=True)
 
     def step():
-        p2p(q, k, v, bt, lens, max_seq_len=L, gather=True, gathered_out=out)
+        p2p(q, k, v, bt, lens, max_seq_len=L, workspace=ws, gather=True, gathered_out=out)
 
     g = torch.Generator().manual_seed(43)
     for it in range(4):  # eager calls: the device-side call counter advances in lockstep
@@ -202,9 +206,9 @@ _P2P_GATHER_SCRIPT = textwrap.dedent(
         torch.cuda.synchronize()
         full.seq_lens.copy_(lens.cpu())
         assert_attention_close(out, oracle_dense(q_cpu, full), torch.float16, "rank %d eager %d" % (rank, it))
-        ref = nccl(q, k, v, bt, lens, max_seq_len=L, gather=True)
+        ref = nccl(q, k, v, bt, lens, max_seq_len=L, workspace=ws, gather=True)
         assert torch.equal(ref, out), "fused p2p and NCCL gathers differ"
-        local = nccl(q, k, v, bt, lens, max_seq_len=L)
+        local = nccl(q, k, v, bt, lens, max_seq_len=L, workspace=ws)
         assert torch.equal(p2p.gather(local), out), "fused and unfused p2p gathers differ"
     st = torch.cuda.Stream()
     st.wait_stream(torch.cuda.current_stream())
