@@ -12,9 +12,11 @@ matching slice of the output.  Block tables and lengths are replicated.  No
 data moves between ranks to compute a rank's heads, so a head-sharded
 consumer (a tensor-parallel o_proj) needs no collective at all; an
 all-gather of the per-head outputs is offered only for consumers that need
-every head on every rank (``gather=True``): NCCL's, or one kernel of ours
-that stores each rank's heads into every peer's memory over NVLink
-(``exchange="p2p"``, ``dk_gather_heads``).
+every head on every rank (``gather=True``): NCCL's, or ours over NVLink
+peer memory (``exchange="p2p"``), where the decode's own output stores put
+each rank's heads into every peer's receive buffer and one small kernel
+completes the collective (``dk_paged_attention_decode_gather``;
+``dk_gather_heads`` gathers outputs computed elsewhere).
 
 Sequence sharding, for models whose KV heads cannot be split (MQA, or
 fewer KV heads than GPUs) and for long contexts at small batch: block ``j``
@@ -109,8 +111,9 @@ class ShardedPagedAttention:
     ``attention_fn`` defaults to :func:`decodekernels_b200.paged_attention_decode`
     (the sm_100a kernels); tests of the host-side logic on CPU ranks pass the
     CPU oracle instead.  ``exchange`` chooses the gather: ``"nccl"``
-    (``all_gather_into_tensor``) or ``"p2p"`` (``dk_gather_heads`` over
-    symmetric memory; CUDA ranks of one node, waits bounded by
+    (``all_gather_into_tensor``) or ``"p2p"`` (over symmetric memory: fused
+    into the decode with the native kernels, ``dk_paged_attention_decode_gather``,
+    else ``dk_gather_heads`` after it; CUDA ranks of one node, waits bounded by
     ``wait_limit_ms``, 0 = 2 s).
     """
 
