@@ -6,8 +6,8 @@
                                 DecodeKernels tree's ``csrc/`` on the include
                                 path -> oracle/_ref/libdk_ref_kernel.so.  Runs
                                 only where that tree exists (``DK_REFERENCE_DIR``,
-                                default ``/root/reference``); elsewhere it keeps
-                                a prebuilt library if one is present.
+                                else the build container's checkout); elsewhere
+                                it keeps a prebuilt library if one is present.
 """
 
 from __future__ import annotations

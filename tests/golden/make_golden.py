@@ -1,7 +1,7 @@
 """Write the golden vectors that pin the CPU oracle and the CUDA path.
 
 Run in a container that has the DecodeKernels reference tree mounted
-(default ``/root/reference``, override with ``DK_REFERENCE_DIR``):
+(``DK_REFERENCE_DIR``, else the build container's checkout):
 
     python tests/golden/make_golden.py
 

@@ -13,6 +13,7 @@
 import ctypes
 import os
 import subprocess
+import tempfile
 import sys
 import textwrap
 
@@ -175,7 +176,7 @@ _SCRIPT = textwrap.dedent(
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_nccl_ranks_exchange_partials():
     script = _SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
-    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    path = tempfile.gettempdir()
     f = os.path.join(path, "seq_sharded_nccl_case.py")
     with open(f, "w") as fh:
         fh.write(script)
@@ -275,7 +276,7 @@ _P2P_SCRIPT = textwrap.dedent(
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_ranks_peer_memory_exchange():
     script = _P2P_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
-    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    path = tempfile.gettempdir()
     f = os.path.join(path, "seq_sharded_p2p_case.py")
     with open(f, "w") as fh:
         fh.write(script)

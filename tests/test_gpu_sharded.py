@@ -9,6 +9,7 @@
 
 import os
 import subprocess
+import tempfile
 import sys
 import textwrap
 
@@ -79,7 +80,7 @@ _SCRIPT = textwrap.dedent(
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_two_nccl_ranks_gather():
     script = _SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
-    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    path = tempfile.gettempdir()
     f = os.path.join(path, "sharded_nccl_case.py")
     with open(f, "w") as fh:
         fh.write(script)
@@ -239,7 +240,7 @@ def test_two_ranks_peer_memory_gather():
     separate peer-memory gather and NCCL's, and the oracle, eagerly and under
     CUDA-graph replay."""
     script = _P2P_GATHER_SCRIPT.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
-    path = os.path.join(ROOT, "gpurun_out") if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "/tmp"
+    path = tempfile.gettempdir()
     f = os.path.join(path, "head_sharded_p2p_case.py")
     with open(f, "w") as fh:
         fh.write(script)
