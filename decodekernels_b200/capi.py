@@ -329,7 +329,8 @@ def decode(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out,
     return rc
 
 
-def decode_noalloc(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, stream=None) -> int:
+def decode_noalloc(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, stream=None,
+                   flags: int = 0, k_scale: float = 1.0, v_scale: float = 1.0) -> int:
     """dk_paged_attention_decode_noalloc: the decode for callers that cannot
     allocate device memory (plugin hosts and runtimes that own all memory
     besides a kernel's inputs and outputs, FFI hosts without a CUDA
@@ -339,7 +340,8 @@ def decode_noalloc(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_l
     """
     import torch
 
-    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, None)
+    a = make_args(q, k_cache, v_cache, block_tables, seq_lens, scale, max_seq_len, out, None, 0, False, flags,
+                  k_scale, v_scale)
     if stream is None:
         stream = torch.cuda.current_stream(q.device).cuda_stream if q.is_cuda else 0
     rc = load().dk_paged_attention_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(stream))

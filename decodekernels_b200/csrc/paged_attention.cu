@@ -84,12 +84,18 @@ constexpr int round_up(long long a, long long b) { return static_cast<int>(((a +
 #define DK_TMA_WARPS_D256 2
 #endif
 
+// Resident CTAs per SM the head_dim-64 instances' registers must allow: six
+// fit its 33 KB ring, and without the bound the compact instance spilled
+// (72 registers, 8 bytes); with it both use 64 registers and spill nothing.
+#ifndef DK_TMA_MIN_CTAS_D64
+#define DK_TMA_MIN_CTAS_D64 6
+#endif
 template <int D>
 struct TmaShape {
   static constexpr int kStages = D == 64 ? DK_TMA_STAGES_D64 : (D == 128 ? DK_TMA_STAGES_D128 : DK_TMA_STAGES_D256);
   static constexpr int kWarps = D == 64 ? DK_TMA_WARPS_D64 : (D == 128 ? DK_TMA_WARPS_D128 : DK_TMA_WARPS_D256);
   static constexpr int kSlices = 1;
-  static constexpr int kMinCtas = 0;
+  static constexpr int kMinCtas = D == 64 ? DK_TMA_MIN_CTAS_D64 : 0;
   using Cfg = TmaConfig<D, kStages, kWarps>;
 };
 
@@ -560,11 +566,12 @@ int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
     }
     return 0;
   }
-  if (pl.path == DK_PATH_TMA_MMA) {
+  if (pl.path == DK_PATH_TMA_MMA) {  // the dense-grid instance launch_tma runs
     using Shape = TmaShape<D>;
     static bool attr_done[kMaxDevices] = {false};
-    return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps>, Shape::Cfg::kThreads,
-                        Shape::Cfg::kSmemBytes, dev, attr_done);
+    return occupancy_of(
+        paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, false, Shape::kSlices, Shape::kMinCtas>,
+        Shape::Cfg::kThreads, Shape::Cfg::kSmemBytes, dev, attr_done);
   }
   static bool attr_done[kMaxDevices] = {false};
   return fp8 ? occupancy_of(paged_decode_simt_kernel<T, D, uint8_t>, kSimtThreads, SimtConfig<D>::kSmemBytes, dev,
@@ -756,9 +763,11 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
 // address comes from cudaGetSymbolAddress, once per device.
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) float g_noalloc_scratch[DK_NOALLOC_SCRATCH_BYTES / sizeof(float)];
-// Merge counters of the no-allocation path (zero at load; every completed
-// call leaves them zero).  Calls with more (sequence, KV head) pairs use the
-// separate merge kernel.
+// Merge counters of the no-allocation path.  A call that completes leaves the
+// ones it used at zero, but one whose bounded wait gave up may not (its CTA
+// skips the rest of its items), so every call that uses them clears its range
+// with cudaMemsetAsync on its stream first.  Calls with more (sequence, KV
+// head) pairs use the separate merge kernel.
 constexpr int kNoallocCounters = 1 << 18;
 static __device__ __align__(256) int g_noalloc_counters[kNoallocCounters];
 
@@ -1066,12 +1075,20 @@ int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t s
     a.max_logits = base + rows * a.head_dim;
     a.exp_sums = a.max_logits + rows;
     a.max_partitions = pl.num_partitions;
-    if (static_cast<long long>(a.num_seqs) * a.num_kv_heads <= dkb::kNoallocCounters) {
+    const long long pairs = static_cast<long long>(a.num_seqs) * a.num_kv_heads;
+    if (pairs <= dkb::kNoallocCounters) {
       a.merge_counters = counters;  // one launch when the merge is small
       const int fixed = a.partition_size;
       a.partition_size = pl.partition_size;  // same partitions; only the merge choice is re-planned
       dkb::make_plan(a, dev, &pl);
       a.partition_size = fixed;
+      if (pl.launches == 1) {
+        // Start from zero whatever an earlier call left behind (a wait that
+        // gave up leaves its pairs' counts part-way); a memset allocates nothing.
+        ce = cudaMemsetAsync(counters, 0, static_cast<size_t>(pairs) * sizeof(int),
+                             reinterpret_cast<cudaStream_t>(stream));
+        if (ce != cudaSuccess) return dkb::fail_cuda(ce, "cudaMemsetAsync(no-allocation merge counters)");
+      }
     }
   }
   return dkb::launch(a, pl, dev, reinterpret_cast<cudaStream_t>(stream));

@@ -162,8 +162,15 @@ DK_API int dk_paged_attention_decode(const DkPagedAttnArgs* args, dk_stream_t st
  * The first call on each device looks up the scratch's device address (with
  * that device current); make that first call before any stream capture.
  * All calls share the one array: calls that can overlap on the GPU (other
- * streams, other threads) race on it.  Nothing in it needs to start at zero:
- * each call writes every scratch row it reads.
+ * streams, other threads) race on it.  The float partials need no clearing:
+ * each call writes every scratch row it reads.  Calls with few enough
+ * (sequence, KV head) pairs also use library-owned merge counters (one int32
+ * per pair, at most 2^18 pairs), which must be zero when the kernel starts; a
+ * completed call leaves them zero, but one whose bounded wait gave up
+ * (dk_device_wait_timeouts rises) may not, so every such call first clears
+ * the counters it uses with cudaMemsetAsync on `stream` (one memset node
+ * before the kernel; it allocates nothing).  A later call therefore never
+ * inherits a failed call's counts.
  */
 #define DK_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 DK_API int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t stream);

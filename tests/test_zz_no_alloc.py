@@ -9,7 +9,11 @@ keeps the split-K partials in the library's static scratch array.
 These tests call it through the C ABI and compare it with the regular entry
 point (which gets a workspace allocated here), on two calls in a row with
 different batches, so the second call starts from the first call's leftover
-scratch.  The file is named to run last; it passes alone and after the rest.
+scratch.  Small calls also use the library's own merge counters; the compact
+grid cases (an e4m3 cache, and DK_FLAG_PERSISTENT) run the same call three
+times and require identical results, which holds only if the counters are
+zero whenever a call starts.  The file is named to run last; it passes alone
+and after the rest.
 """
 
 import pytest
@@ -18,7 +22,7 @@ import torch
 import decodekernels_b200 as dk
 from decodekernels_b200 import capi
 from decodekernels_b200.testing import make_paged_kv
-from gpu_helpers import alloc_ws, assert_attention_close, oracle_dense
+from gpu_helpers import alloc_ws, assert_attention_close, fp8_caches, oracle_dense, oracle_dense_fp8
 
 pytestmark = [
     pytest.mark.gpu,
@@ -33,12 +37,14 @@ def _batch(seq_lens, seed, dtype, layout):
     return q, kv
 
 
-def _regular(q, kv, max_len):
+def _regular(q, kv, max_len, k=None, v=None, flags=0, scales=(1.0, 1.0)):
     n, hq, d = q.shape
-    parts = capi.num_partitions(n, kv.k_cache.shape[2], d, kv.block_size, max_len)
+    k = kv.k_cache if k is None else k
+    v = kv.v_cache if v is None else v
+    parts = capi.num_partitions(n, k.shape[2], d, kv.block_size, max_len)
     out = torch.full_like(q, float("nan"))
-    capi.decode(q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out,
-                alloc_ws(n, hq, d, parts, q.device))
+    capi.decode(q, k, v, kv.block_tables, kv.seq_lens, d**-0.5, max_len, out, alloc_ws(n, hq, d, parts, q.device),
+                flags=flags, k_scale=scales[0], v_scale=scales[1])
     return out
 
 
@@ -85,3 +91,45 @@ def test_noalloc_refuses_a_workspace():
 
     rc = capi.load().dk_paged_attention_decode_noalloc(ctypes.byref(args), None)
     assert rc == 1 and "takes no workspace" in capi.last_error()
+
+
+KS, VS = 0.02, 0.015
+
+
+@pytest.mark.parametrize("case", ["e4m3_compact", "persistent"])
+def test_noalloc_compact_grid_with_library_counters(case):
+    # Few (sequence, KV head) pairs and long sequences: 16 partitions of 1024
+    # tokens, a merge small enough for the single-launch merge, so the call
+    # uses the library-owned merge counters.  e4m3 caches take the compact grid
+    # by default there; DK_FLAG_PERSISTENT takes it (one wave, several items
+    # per CTA) for a 16-bit cache.  The same call runs twice more: equal
+    # results show the counters were zero at the start of every call.
+    lens = [16384, 9000, 0, 1, 12000, 3000, 16000, 777]
+    q, kv = _batch(lens, seed=5, dtype=torch.float16, layout="vllm")
+    max_len = max(lens)
+    if case == "e4m3_compact":
+        k, v = fp8_caches(kv, "vllm", KS, VS)
+        flags, scales = 0, (KS, VS)
+        want = oracle_dense_fp8(q, kv, k, v, KS, VS)
+    else:
+        k, v = kv.k_cache, kv.v_cache
+        flags, scales = capi.DK_FLAG_PERSISTENT, (1.0, 1.0)
+        want = oracle_dense(q, kv)
+    counters = torch.zeros(len(lens) * 8, dtype=torch.int32, device="cuda")
+    parts = capi.num_partitions(len(lens), 8, 128, 16, max_len)
+    plan = capi.plan(q, k, v, kv.block_tables, kv.seq_lens, 128**-0.5, max_len, torch.empty_like(q),
+                     (*alloc_ws(len(lens), 32, 128, parts, q.device), counters), flags=flags, k_scale=scales[0],
+                     v_scale=scales[1])
+    assert plan["split"] == 1 and plan["launches"] == 1 and plan["num_partitions"] >= 16, plan
+    regular = _regular(q, kv, max_len, k, v, flags, scales)
+    runs = []
+    for _ in range(3):
+        got = torch.full_like(q, float("nan"))
+        capi.decode_noalloc(q, k, v, kv.block_tables, kv.seq_lens, 128**-0.5, max_len, got, flags=flags,
+                            k_scale=scales[0], v_scale=scales[1])
+        torch.cuda.synchronize()
+        runs.append(got)
+    assert torch.equal(runs[0], runs[1]) and torch.equal(runs[1], runs[2]), "repeated no-alloc calls differ"
+    assert_attention_close(runs[0], regular.float().cpu().numpy(), q.dtype, f"{case}: no-alloc vs regular")
+    assert_attention_close(runs[0], want, q.dtype, f"{case}: no-alloc vs oracle")
+    assert capi.wait_timeouts(0) == 0
