@@ -100,10 +100,56 @@ def build_torch_binding(force: bool = False, verbose: bool = False) -> Path:
     return TORCH_LIB
 
 
+def ptxas_report() -> list[dict]:
+    """Compile the library's device code once more with ``-Xptxas -v`` (into
+    a temporary directory, discarded) and return what ptxas reports for each
+    kernel instance: ``name`` (demangled), ``registers``, ``stack_bytes``,
+    ``spill_stores``, ``spill_loads``.  The zero-spill check of the test suite
+    reads this (DecodeKernels enforces the same per architecture in
+    ``tools/compile_check.sh:17-40``)."""
+    import re
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        cmd = [_nvcc(), *ARCH_FLAGS, "-O3", "-std=c++17", "-cubin", "-Xptxas=-v", "-o",
+               str(Path(tmp) / "dk.cubin"), str(CSRC / "paged_attention.cu")]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ptxas report build failed:\n{r.stdout}{r.stderr}")
+    kernels, cur = [], None
+    for line in (r.stdout + r.stderr).splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            cur = {"mangled": m.group(1), "registers": None, "stack_bytes": None, "spill_stores": None,
+                   "spill_loads": None}
+            kernels.append(cur)
+            continue
+        if cur is None:
+            continue
+        m = re.search(r"(\d+) bytes stack frame, (\d+) bytes spill stores, (\d+) bytes spill loads", line)
+        if m:
+            cur["stack_bytes"], cur["spill_stores"], cur["spill_loads"] = (int(x) for x in m.groups())
+        m = re.search(r"Used (\d+) registers", line)
+        if m:
+            cur["registers"] = int(m.group(1))
+    names = [k["mangled"] for k in kernels]
+    if shutil.which("c++filt") and names:
+        out = subprocess.run(["c++filt"], input="\n".join(names), capture_output=True, text=True).stdout.split("\n")
+        for k, n in zip(kernels, out):
+            k["name"] = n.strip() or k["mangled"]
+    for k in kernels:
+        k.setdefault("name", k["mangled"])
+    return kernels
+
+
 def build_all(force: bool = False, verbose: bool = False) -> None:
     build_cuda_library(force=force, verbose=verbose)
     build_torch_binding(force=force, verbose=verbose)
 
 
 if __name__ == "__main__":
-    build_all(force="--force" in sys.argv, verbose=True)
+    if "--ptxas" in sys.argv:
+        for k in ptxas_report():
+            print(f"{k['registers']:4d} regs  {k['spill_stores']:3d}/{k['spill_loads']:3d} B spilled  {k['name']}")
+    else:
+        build_all(force="--force" in sys.argv, verbose=True)

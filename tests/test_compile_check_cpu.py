@@ -1,0 +1,49 @@
+"""CPU: the zero-spill compile check.  Every kernel instance of libdk_b200.so,
+compiled for sm_100a as the library is, must spill nothing and keep no local
+stack, as ptxas reports with -v (DecodeKernels makes the same check per
+architecture: tools/compile_check.sh:17-40).  A spill on the decode's hot
+loop turns register traffic into local-memory traffic on the HBM-bound path."""
+
+import shutil
+from pathlib import Path
+
+import pytest
+
+from decodekernels_b200 import build
+
+pytestmark = pytest.mark.skipif(shutil.which(build._nvcc()) is None and not Path(build._nvcc()).exists(),
+                                reason="needs nvcc")
+
+
+@pytest.fixture(scope="module")
+def report():
+    return build.ptxas_report()
+
+
+def test_every_instance_was_reported(report):
+    names = [k["name"] for k in report]
+    # 16-bit and e4m3 TMA partition kernels (dense and compact grids), CUDA-core
+    # partition kernels, merges, exchange, gather and cache-write kernels
+    assert sum("paged_decode_tma_kernel" in n for n in names) == 20
+    assert sum("paged_decode_simt_kernel" in n for n in names) == 12
+    assert len(report) >= 59
+    assert all(k["registers"] is not None and k["spill_stores"] is not None for k in report)
+
+
+def test_no_instance_spills(report):
+    bad = [f"{k['name']}: {k['registers']} registers, {k['stack_bytes']} B stack, {k['spill_stores']} B spill stores, "
+           f"{k['spill_loads']} B spill loads" for k in report
+           if k["spill_stores"] or k["spill_loads"] or k["stack_bytes"]]
+    assert not bad, "\n".join(bad)
+
+
+def test_partition_kernels_fit_their_planned_residency(report):
+    # The planner's occupancy assumptions: at head_dim 64 six CTAs of 160
+    # threads per SM (the ring's limit), at 128 three of 160, at 256 three of 96.
+    threads = {64: 160, 128: 160, 256: 96}
+    ctas = {64: 6, 128: 3, 256: 3}
+    for k in report:
+        if "paged_decode_tma_kernel<" not in k["name"]:
+            continue
+        d = int(k["name"].split("paged_decode_tma_kernel<")[1].split(",")[1])
+        assert k["registers"] * threads[d] * ctas[d] <= 65536, k
