@@ -6,7 +6,9 @@
                           source tree (oracle/_ref/libdk_ref_kernel.so), run on
                           the same device tensors as this library.
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use it.
+Only tests/, __graft_entry__.smoke() and bench.py use it -- bench.py as the
+checker of its outputs before timing, as the timed CPU baseline, and to time
+the reference's own kernel beside this library's for comparison.
 """
 
 from __future__ import annotations
@@ -47,6 +49,8 @@ class DkOracleArgs(ctypes.Structure):
         ("dtype", ctypes.c_int32),
         ("num_threads", ctypes.c_int32),
         ("scale", ctypes.c_float),
+        ("threads_used", ctypes.c_int32),
+        ("units", ctypes.c_int32),
     ]
 
 
@@ -123,10 +127,13 @@ def _dtype_code(t) -> int:
     return {torch.float16: 0, torch.bfloat16: 1}[t.dtype]
 
 
-def dense_c(q, k_cache, v_cache, block_tables, seq_lens, scale=None, num_threads: int = 0) -> np.ndarray:
+def dense_c(q, k_cache, v_cache, block_tables, seq_lens, scale=None, num_threads: int = 0,
+            info: dict | None = None) -> np.ndarray:
     """Dense attention on the CPU through the C oracle.  Inputs are CPU torch
     tensors (fp16/bf16 q and caches, any strides); returns float32 numpy
-    ``[num_seqs, Hq, D]``."""
+    ``[num_seqs, Hq, D]``.  ``num_threads`` > 0 sets the OpenMP team size
+    (0: OpenMP's default, which OMP_NUM_THREADS controls); ``info`` receives
+    ``threads_used`` and ``units`` (parallel work units)."""
     import torch
 
     n, hq, d = q.shape
@@ -150,6 +157,8 @@ def dense_c(q, k_cache, v_cache, block_tables, seq_lens, scale=None, num_threads
     rc = oracle_lib().dk_oracle_paged_attention(ctypes.byref(a))
     if rc != 0:
         raise RuntimeError(f"dk_oracle_paged_attention failed ({rc})")
+    if info is not None:
+        info["threads_used"], info["units"] = int(a.threads_used), int(a.units)
     return out
 
 

@@ -1,7 +1,8 @@
 """CPU oracle for sequence-sharded decode.  TEST INFRASTRUCTURE, NOT PRODUCT.
 
-Only ``tests/`` may import this module, as the checker (and, in the CPU
-``gloo`` tests of the sharding logic, as the stand-in for the CUDA kernels).
+Only ``tests/`` and ``bench.py``'s parity check of the sequence-sharded
+exchange may import this module, as the checker (and, in the CPU ``gloo``
+tests of the sharding logic, as the stand-in for the CUDA kernels).
 
 DecodeKernels runs on one GPU; splitting a sequence's tokens across GPUs is
 new here, so this module restates the mathematics the split relies on, in

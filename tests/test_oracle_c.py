@@ -42,3 +42,17 @@ def test_c_oracle_half_conversion_is_exact():
 
 def test_c_oracle_threads():
     assert native.max_threads() >= 1
+
+
+def test_c_oracle_head_split_is_bit_identical():
+    # More threads than (sequence, KV head) pairs: the work is split per query
+    # head, which must not change a single bit of the result.
+    case = next(c for c in HALF if c["name"] == "c1")
+    q, kv = build(case)
+    args = (q, kv.k_cache, kv.v_cache, kv.block_tables, kv.seq_lens)
+    one, many = {}, {}
+    a = native.dense_c(*args, scale=case["scale"], num_threads=1, info=one)
+    b = native.dense_c(*args, scale=case["scale"], num_threads=64, info=many)
+    assert one == {"threads_used": 1, "units": 4 * 8}
+    assert many["units"] == 4 * 32 and many["threads_used"] >= 1
+    np.testing.assert_array_equal(a, b)
