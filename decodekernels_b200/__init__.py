@@ -39,4 +39,4 @@ __all__ = [
     "paged_attention_decode_lse",
     "reshape_and_cache",
 ]
-__version__ = "0.5.0"
+__version__ = "0.8.0"

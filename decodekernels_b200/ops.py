@@ -10,8 +10,9 @@ inside CUDA graphs.
 Differences that stay within the reference's contract:
 
 * ``alloc_workspace`` sizes the split-K workspace for this library's per-shape
-  planner (partitions of 128..512 tokens chosen to fill all SMs), which is
-  never smaller than the reference's ``ceil(max_seq_len / 512)``.  Optional
+  planner (partitions of 512 KB to 2 MB of K+V -- 1024 to 4096 tokens at
+  head_dim 128 with 16-bit caches -- chosen to fill all SMs), and never
+  smaller than the reference's ``ceil(max_seq_len / 512)`` partitions.  Optional
   keyword ``num_kv_heads`` sizes it exactly; without it the size covers any
   head count.
 * A non-empty workspace is also used when ``max_seq_len <= 512`` (small

@@ -1,12 +1,13 @@
-"""vLLM general-plugin entry point (``vllm.general_plugins``).
+"""Entry point that vLLM calls through its ``vllm.general_plugins`` group.
 
-vLLM imports this in every process it starts (API server, engine core,
-workers).  It is a no-op unless ``DECODE_KERNELS_VLLM=1``, so installing the
-package never changes vLLM's behaviour by itself (the reference's switches,
-``decode_kernels/vllm_plugin.py:14-20``):
-
-    DECODE_KERNELS_VLLM=1             enable
-    DECODE_KERNELS_OPS=attention      which ops to swap (default: attention)
+vLLM runs every registered general plugin in each of its processes, so this
+function must stay cheap and must not change anything on its own: it returns
+at once unless the environment variable ``DECODE_KERNELS_VLLM`` is ``1``.
+When it is, the attention forward of vLLM's FlashAttention backend is
+patched (``vllm_patch.apply``) for the op names listed, comma-separated, in
+``DECODE_KERNELS_OPS`` (default ``attention``, the only op this library
+implements; other names are logged and skipped).  The variable names and
+their meaning are DecodeKernels' (``decode_kernels/vllm_plugin.py:14-20``).
 """
 
 import os
