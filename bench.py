@@ -516,7 +516,56 @@ def _vs_reference_kernel(batch, out, dev, ours_fn) -> dict:
             "method": "median of 100 calls, 256 MB L2 flush before each, 10 warm-up calls"}
 
 
-def _also(names, steps, warmup, dev, peaks) -> dict:
+def _flashinfer(batch, out, dev, ours_us: float) -> dict:
+    """FlashInfer's batch decode (the baseline of DecodeKernels' own benchmark,
+    benchmarks/bench_kernels.py:60-85) on the same batch: CUDA-core and
+    tensor-core variants, each on contiguous NHD copies of the caches (its
+    native layout; the copies are made before timing), checked against this
+    library's output and timed the reference benchmark's way."""
+    import itertools
+
+    import numpy as np
+    import torch
+
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001
+        return {"error": f"flashinfer import failed: {e}"[:200]}
+    if batch.config.kv_fp8 or min(batch.lens) <= 0:
+        return {"error": "skipped: e4m3 caches or empty sequences"}
+    q, kv = batch.q, batch.kv
+    n, hq, d = q.shape
+    hkv, bs = kv.k_cache.shape[2], kv.block_size
+    blocks = [-(-L // bs) for L in batch.lens]
+    indptr = torch.tensor([0] + list(itertools.accumulate(blocks)), dtype=torch.int32, device=dev)
+    indices = torch.cat([kv.block_tables[i, :b] for i, b in enumerate(blocks)]).to(torch.int32)
+    last = torch.tensor([(L - 1) % bs + 1 for L in batch.lens], dtype=torch.int32, device=dev)
+    k_nhd, v_nhd = kv.k_cache.contiguous(), kv.v_cache.contiguous()
+    ws = torch.zeros(128 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    res = {"version": getattr(flashinfer, "__version__", "?"), "ours_us_same_method": _sig(ours_us)}
+    for tc in (False, True):
+        key = "tensor_cores" if tc else "cuda_cores"
+        try:
+            w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout="NHD", use_tensor_cores=tc)
+            w.plan(indptr, indices, last, hq, hkv, d, bs, q_data_type=q.dtype, kv_data_type=q.dtype,
+                   sm_scale=d**-0.5)
+
+            def fn():
+                return w.run(q, (k_nhd, v_nhd))
+
+            o = fn()
+            torch.cuda.synchronize()
+            diff = float(np.abs(o.float().cpu().numpy() - out.float().cpu().numpy()).max())
+            t = _time_reference_method(fn, dev)
+            res[key] = {"us": _sig(t["median_us"]), "ours_speedup": _sig(t["median_us"] / ours_us),
+                        "max_abs_diff_vs_ours": _sig(diff, 3)}
+        except Exception as e:  # noqa: BLE001
+            res[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    del k_nhd, v_nhd, ws
+    return res
+
+
+def _also(names, steps, warmup, dev, peaks, flashinfer: bool = False) -> dict:
     """Other workloads on this GPU: device-timed TB/s and roofline fraction
     (same method as the headline), a parity spot check, and the comparison
     with the reference's kernel."""
@@ -553,6 +602,9 @@ def _also(names, steps, warmup, dev, peaks) -> dict:
                  "l2_flush": flush is not None, "parity_ok": parity["ok"],
                  "parity_max_abs": _sig(parity["max_abs"], 3)}
         entry.update(_vs_reference_kernel(batch, out, dev, step))
+        if flashinfer:
+            ours_us = entry.get("ours_us_same_method") or _time_reference_method(step, dev)["median_us"]
+            entry["flashinfer"] = _flashinfer(batch, out, dev, ours_us)
         res[name] = entry
         del batch, q, kv, out, ws, flush
         torch.cuda.empty_cache()
@@ -829,7 +881,7 @@ def run_gpu_arm(args) -> None:
         if names:
             del ws, out, q, kv, batch, outs, d_stage, ins  # the headline batch is no longer needed
             torch.cuda.empty_cache()
-            also = _also(names, max(args.steps, 100), args.warmup, dev, _peaks())
+            also = _also(names, max(args.steps, 100), args.warmup, dev, _peaks(), args.flashinfer)
 
     if rank == 0:
         step_s = device_s / args.steps
@@ -905,6 +957,9 @@ def main() -> None:
                     help="N=1: other workloads timed after the headline (comma-separated; empty for none)")
     ap.add_argument("--no-also", action="store_true",
                     help="skip the reference-kernel comparison and the other workloads")
+    ap.add_argument("--flashinfer", action="store_true",
+                    help="N=1: also time FlashInfer's batch decode on the 16-bit workloads under --also (it may "
+                         "compile kernels on first use)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
