@@ -6,7 +6,8 @@
                                 DecodeKernels tree's ``csrc/`` on the include
                                 path -> oracle/_ref/libdk_ref_kernel.so.  Runs
                                 only where that tree exists (``DK_REFERENCE_DIR``,
-                                else the build container's checkout); elsewhere
+                                else a ``reference`` directory beside this
+                                repository's checkout); elsewhere
                                 it keeps a prebuilt library if one is present.
 """
 
@@ -47,7 +48,10 @@ def build_oracle(force: bool = False) -> Path:
 
 
 def reference_dir() -> Path:
-    return Path(os.environ.get("DK_REFERENCE_DIR", "/root/reference"))
+    """The DecodeKernels source tree: ``DK_REFERENCE_DIR``, else ``../reference``
+    relative to this repository's root."""
+    env = os.environ.get("DK_REFERENCE_DIR")
+    return Path(env) if env else HERE.parent.parent / "reference"
 
 
 def build_reference_kernel(force: bool = False) -> Path | None:

@@ -1,7 +1,8 @@
 """Write the golden vectors that pin the CPU oracle and the CUDA path.
 
 Run in a container that has the DecodeKernels reference tree mounted
-(``DK_REFERENCE_DIR``, else the build container's checkout):
+(``DK_REFERENCE_DIR``, else a ``reference`` directory beside this
+repository's checkout):
 
     python tests/golden/make_golden.py
 
@@ -36,7 +37,8 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("DK_REFERENCE_DIR", "/root/reference"))
+REF = Path(os.environ["DK_REFERENCE_DIR"]) if os.environ.get("DK_REFERENCE_DIR") else \
+    HERE.parent.parent.parent / "reference"
 
 sys.path.insert(0, str(HERE.parent.parent))
 from decodekernels_b200.testing import tensor_digest  # noqa: E402
