@@ -22,7 +22,6 @@
 #include "decode_params.cuh"
 #include "merge_partitions.cuh"
 #include "partition_simt.cuh"
-#include "partition_tc.cuh"
 #include "partition_tma.cuh"
 #include "peer_exchange.cuh"
 #include "reshape_and_cache.cuh"
@@ -138,18 +137,6 @@ struct TmaShapeFp8 {
 };
 
 int tma_tile_fp8(int D) { return D == 128 ? TmaShapeFp8<128>::Cfg::kTile : TmaShapeFp8<256>::Cfg::kTile; }
-
-// e4m3 caches at head_dim 128 on the dense grid run the tcgen05 kernel
-// (partition_tc.cuh): the tensor cores read the e4m3 tiles as they are.
-#ifndef DK_FP8_TC
-#define DK_FP8_TC 1
-#endif
-#ifndef DK_TC_STAGES
-#define DK_TC_STAGES 3
-#endif
-using TcCfg = TcConfig<128, DK_TC_STAGES>;
-static_assert(TcCfg::kTile == TmaShapeFp8<128>::Cfg::kTile, "the tcgen05 kernel keeps the e4m3 tile");
-bool tc_capable(bool fp8, int head_dim) { return DK_FP8_TC && fp8 && head_dim == 128; }
 
 int tma_tile(int D) {
   return D == 64 ? TmaShape<64>::Cfg::kTile : (D == 128 ? TmaShape<128>::Cfg::kTile : TmaShape<256>::Cfg::kTile);
@@ -359,23 +346,6 @@ int ilog2(int x) {
   return r;
 }
 
-// Compact grid (compact_coords): with DK_FLAG_PERSISTENT, and by default for
-// e4m3 caches on the conversion kernel (head_dim 256) when a sequence may
-// span many partitions.  Its CTAs pay a scan of the lengths (one L2 round
-// trip) before their first loads; that is repaid where the consumers' math
-// bounds a CTA (e4m3: c4 80.7 -> ~73 us) but not where HBM does (16-bit c4:
-// 85 -> 89 us).  The tcgen05 kernel runs the dense grid.
-bool plan_compact(const DkPagedAttnArgs& a, const DkPlan& pl) {
-  if (pl.path != DK_PATH_TMA_MMA || a.num_seqs > kCompactMaxSeqs) return false;
-  if (a.flags & DK_FLAG_PERSISTENT) return true;
-  return a.kv_fp8 && !tc_capable(true, a.head_dim) && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1;
-}
-
-// The partition kernel a TMA-path plan runs is the tcgen05 one.
-bool plan_tc(const DkPagedAttnArgs& a, const DkPlan& pl) {
-  return pl.path == DK_PATH_TMA_MMA && tc_capable(a.kv_fp8 != 0, a.head_dim) && !plan_compact(a, pl);
-}
-
 void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   std::memset(pl, 0, sizeof(*pl));
   if (a.num_seqs == 0) {
@@ -413,10 +383,6 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
                                           : (a.head_dim == 64 ? tma_stages<64>()
                                                               : (a.head_dim == 128 ? tma_stages<128>() : tma_stages<256>()));
   pl->smem_bytes = smem_for(pl->path, a.head_dim, a.kv_fp8 != 0);
-  if (plan_tc(a, *pl)) {
-    pl->stages = DK_TC_STAGES;
-    pl->smem_bytes = TcCfg::kSmemBytes;
-  }
   // Merge counters turn the merge into the last partition's epilogue, which
   // saves the merge kernel's launch and latency but costs every partition a
   // release + atomic round trip and leaves each pair's merge to one CTA.
@@ -460,7 +426,6 @@ struct MapKey {
   int64_t sizes[3];
   int rows;
   int col_blocks;
-  int box_cols;
   int dev;
   bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
 };
@@ -483,10 +448,8 @@ int g_map_next = 0;
 // lands in shared memory as [column block][row][128 B], 128-byte swizzled.
 // esz: element size (2, or 1 for e4m3 bytes); a 128-byte column block holds
 // 128 / esz elements.
-// box_cols (0: all col_blocks) is the column blocks one box copies.
 int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, int64_t num_blocks, int block_size,
-              int num_kv_heads, int col_blocks, int rows, int dev, CUtensorMap* out, int esz = 2, int box_cols = 0) {
-  if (box_cols <= 0) box_cols = col_blocks;
+              int num_kv_heads, int col_blocks, int rows, int dev, CUtensorMap* out, int esz = 2) {
   MapKey key;
   std::memset(&key, 0, sizeof(key));
   key.ptr = ptr;
@@ -499,7 +462,6 @@ int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, i
   key.sizes[2] = num_blocks;
   key.rows = rows;
   key.col_blocks = col_blocks;
-  key.box_cols = box_cols;
   key.dev = dev;
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
@@ -522,7 +484,7 @@ int build_map(const void* ptr, int64_t s_block, int64_t s_tok, int64_t s_head, i
                               static_cast<cuuint64_t>(num_kv_heads), static_cast<cuuint64_t>(num_blocks)};
   const cuuint64_t gstride[4] = {legal(block_size, s_tok), 128, legal(num_kv_heads, s_head),
                                  legal(num_blocks, s_block)};
-  const cuuint32_t box[5] = {inner, static_cast<cuuint32_t>(rows), static_cast<cuuint32_t>(box_cols), 1, 1};
+  const cuuint32_t box[5] = {inner, static_cast<cuuint32_t>(rows), static_cast<cuuint32_t>(col_blocks), 1, 1};
   const cuuint32_t estride[5] = {1, 1, 1, 1, 1};
   CUtensorMap map;
   CUresult r = fn(&map, esz == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 5,
@@ -593,15 +555,7 @@ int occupancy_of(Kernel kernel, int threads, int smem, int dev, bool* attr_done)
 }
 
 template <typename T, int D>
-int partition_occupancy(const DkPlan& pl, bool fp8, bool tc, int dev) {
-  if (tc) {
-    if constexpr (D == 128) {
-      static bool attr_done[kMaxDevices] = {false};
-      return occupancy_of(paged_decode_tc_kernel<T, D, DK_TC_STAGES>, TcCfg::kThreads, TcCfg::kSmemBytes, dev,
-                          attr_done);
-    }
-    return 0;
-  }
+int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
   if (pl.path == DK_PATH_TMA_MMA && fp8) {
     if constexpr (D >= 128) {
       using Shape = TmaShapeFp8<D>;
@@ -629,17 +583,15 @@ int plan_occupancy(const DkPagedAttnArgs& a, const DkPlan& pl, int dev) {
   if (dev < 0 || pl.path == DK_PATH_NONE) return 0;
   const bool bf16 = a.dtype == DK_DTYPE_BFLOAT16;
   const bool fp8 = a.kv_fp8 != 0;
-  const bool tc = plan_tc(a, pl);
   switch (a.head_dim) {
     case 64:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 64>(pl, fp8, tc, dev)
-                  : partition_occupancy<__half, 64>(pl, fp8, tc, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 64>(pl, fp8, dev) : partition_occupancy<__half, 64>(pl, fp8, dev);
     case 128:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 128>(pl, fp8, tc, dev)
-                  : partition_occupancy<__half, 128>(pl, fp8, tc, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 128>(pl, fp8, dev)
+                  : partition_occupancy<__half, 128>(pl, fp8, dev);
     default:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 256>(pl, fp8, tc, dev)
-                  : partition_occupancy<__half, 256>(pl, fp8, tc, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 256>(pl, fp8, dev)
+                  : partition_occupancy<__half, 256>(pl, fp8, dev);
   }
 }
 
@@ -685,38 +637,11 @@ int launch_tma(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int 
   return 0;
 }
 
-// The tcgen05 e4m3 kernel: boxes of one 128-byte column block (K, and V --
-// the second column block of a fused K|V map), dense grid.
-template <typename T>
-int launch_tc(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
-  static bool attr_done[kMaxDevices] = {false};
-  auto kernel = paged_decode_tc_kernel<T, 128, DK_TC_STAGES>;
-  cudaError_t e = ensure_smem_attr(kernel, TcCfg::kSmemBytes, dev, attr_done);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(tcgen05 partition kernel)");
-  const int rows = 1 << p.rows_log2;
-  p.kv_fused = kv_fused(a) ? 1 : 0;
-  CUtensorMap kmap, vmap;
-  if (int r = build_map(a.k_cache, a.k_stride_block, a.k_stride_token, a.k_stride_head, a.num_blocks, a.block_size,
-                        a.num_kv_heads, p.kv_fused ? 2 : 1, rows, dev, &kmap, 1, 1))
-    return r;
-  if (p.kv_fused) {
-    vmap = kmap;  // unused
-  } else if (int r = build_map(a.v_cache, a.v_stride_block, a.v_stride_token, a.v_stride_head, a.num_blocks,
-                               a.block_size, a.num_kv_heads, 1, rows, dev, &vmap, 1, 1)) {
-    return r;
-  }
-  e = launch_pdl(kernel, dim3(static_cast<unsigned>(pl.num_ctas)), dim3(TcCfg::kThreads), TcCfg::kSmemBytes, stream,
-                 kmap, vmap, p);
-  return e == cudaSuccess ? 0 : fail_cuda(e, "tcgen05 partition kernel launch");
-}
-
 template <typename T, int D>
 int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
   const dim3 grid(static_cast<unsigned>(pl.num_ctas));  // 1-D, sequence-major (cta_coords)
   cudaError_t e;
-  if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8 && D == 128 && tc_capable(true, D) && !p.compact) {
-    if (int r = launch_tc<T>(a, pl, p, dev, stream)) return r;
-  } else if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
+  if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
     if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
       const int r = p.compact ? launch_tma<T, D, true, true>(a, pl, p, dev, stream)
                               : launch_tma<T, D, true, false>(a, pl, p, dev, stream);
@@ -794,8 +719,17 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.ws_partitions = pl.split ? a.max_partitions : 1;
   p.split = pl.split;
   p.kv_fp8 = a.kv_fp8;
+  // Compact grid (compact_coords) when most CTAs of the dense grid may have no
+  // tokens: many partitions per sequence, and few enough sequences that every
+  // CTA's warp scan of the lengths stays short.
+  // Compact grid (compact_coords): with DK_FLAG_PERSISTENT, and by default
+  // for e4m3 caches when a sequence may span many partitions.  Its CTAs pay a
+  // scan of the lengths (one L2 round trip) before their first loads; that
+  // is repaid where the consumers' math bounds a CTA (e4m3: c4 80.7 ->
+  // ~73 us) but not where HBM does (16-bit c4: 85 -> 89 us).
   const bool persistent = (a.flags & DK_FLAG_PERSISTENT) != 0;
-  p.compact = plan_compact(a, pl) ? 1 : 0;
+  p.compact = pl.path == DK_PATH_TMA_MMA && a.num_seqs <= kCompactMaxSeqs &&
+              (persistent || (a.kv_fp8 && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1));
   p.persistent = p.compact && persistent;
   p.scale_log2 = a.scale * (a.kv_fp8 ? a.k_scale : 1.0f) * kLog2e;
   p.v_scale = a.kv_fp8 ? a.v_scale : 1.0f;

@@ -26,8 +26,7 @@ def test_every_instance_was_reported(report):
     # partition kernels, merges, exchange, gather and cache-write kernels
     assert sum("paged_decode_tma_kernel" in n for n in names) == 20
     assert sum("paged_decode_simt_kernel" in n for n in names) == 12
-    assert sum("paged_decode_tc_kernel" in n for n in names) == 2  # tcgen05 e4m3 kernel, f16 and bf16 queries
-    assert len(report) >= 61
+    assert len(report) >= 59
     assert all(k["registers"] is not None and k["spill_stores"] is not None for k in report)
 
 
@@ -40,13 +39,10 @@ def test_no_instance_spills(report):
 
 def test_partition_kernels_fit_their_planned_residency(report):
     # The planner's occupancy assumptions: at head_dim 64 six CTAs of 160
-    # threads per SM (the ring's limit), at 128 three of 160, at 256 three of 96;
-    # the tcgen05 e4m3 kernel two of 192.
+    # threads per SM (the ring's limit), at 128 three of 160, at 256 three of 96.
     threads = {64: 160, 128: 160, 256: 96}
     ctas = {64: 6, 128: 3, 256: 3}
     for k in report:
-        if "paged_decode_tc_kernel<" in k["name"]:
-            assert k["registers"] * 192 * 2 <= 65536, k
         if "paged_decode_tma_kernel<" not in k["name"]:
             continue
         d = int(k["name"].split("paged_decode_tma_kernel<")[1].split(",")[1])
