@@ -882,11 +882,10 @@ int launch_peer_exchange(const DkPeerExchangeArgs& a, int dev, cudaStream_t stre
   const long long want = std::max<long long>(std::max<long long>(1, (pairs + 7) / 8),
                                              (p.block_floats / 4 + kExchangeThreads - 1) / kExchangeThreads);
   const dim3 grid(static_cast<unsigned>(std::min<long long>(want, 2LL * num_sms(dev))));
-  if (a.dtype == DK_DTYPE_BFLOAT16)
-    peer_exchange_merge_kernel<__nv_bfloat16, D><<<grid, kExchangeThreads, 0, stream>>>(p);
-  else
-    peer_exchange_merge_kernel<__half, D><<<grid, kExchangeThreads, 0, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = a.dtype == DK_DTYPE_BFLOAT16
+                            ? launch_pdl(peer_exchange_merge_kernel<__nv_bfloat16, D>, grid, dim3(kExchangeThreads), 0,
+                                         stream, p)
+                            : launch_pdl(peer_exchange_merge_kernel<__half, D>, grid, dim3(kExchangeThreads), 0, stream, p);
   return e == cudaSuccess ? 0 : fail_cuda(e, "peer exchange kernel launch");
 }
 
@@ -939,8 +938,7 @@ int launch_peer_gather(const DkPeerGatherArgs& a, int dev, cudaStream_t stream, 
   const long long chunks = p.slot_elems / 8;
   const long long want = std::max<long long>(1, (chunks + kExchangeThreads - 1) / kExchangeThreads);
   const dim3 grid(static_cast<unsigned>(std::min<long long>(want, 2LL * num_sms(dev))));
-  peer_gather_kernel<<<grid, kExchangeThreads, 0, stream>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e = launch_pdl(peer_gather_kernel, grid, dim3(kExchangeThreads), 0, stream, p);
   return e == cudaSuccess ? 0 : fail_cuda(e, "peer gather kernel launch");
 }
 

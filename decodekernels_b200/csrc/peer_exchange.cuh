@@ -59,6 +59,9 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_exchange_merge_kernel(c
   __shared__ uint32_t s_epoch;
   __shared__ int s_last;
   const int tid = threadIdx.x;
+  // Launched as a programmatic dependent of the decode that wrote `partial`:
+  // scheduled while it drains, everything below waits for its completion.
+  pdl_wait_primary();
   if (tid == 0) s_epoch = p.state[0] + 1;  // nothing advances state[0] before every CTA has merged
   __syncthreads();
   const uint32_t e = s_epoch;
@@ -184,6 +187,9 @@ __global__ void __launch_bounds__(kExchangeThreads) peer_gather_kernel(const Pee
   __shared__ uint32_t s_epoch;
   __shared__ int s_last;
   const int tid = threadIdx.x;
+  // Launched as a programmatic dependent of the decode whose output rows it
+  // gathers (or pushed into the slots): everything below waits for it.
+  pdl_wait_primary();
   if (tid == 0) s_epoch = p.state[0] + 1;  // nothing advances state[0] before every CTA has copied
   __syncthreads();
   const uint32_t e = s_epoch;
