@@ -38,12 +38,13 @@ def test_no_instance_spills(report):
 
 
 def test_partition_kernels_fit_their_planned_residency(report):
-    # The planner's occupancy assumptions: at head_dim 64 six CTAs of 160
-    # threads per SM (the ring's limit), at 128 three of 160, at 256 three of 96.
-    threads = {64: 160, 128: 160, 256: 96}
+    # The planner's occupancy assumptions: at head_dim 64 six CTAs per SM (the
+    # ring's limit), at 128 and 256 three; a CTA has WARPS consumer warps and a
+    # producer warp (WARPS is the 4th template argument).
     ctas = {64: 6, 128: 3, 256: 3}
     for k in report:
         if "paged_decode_tma_kernel<" not in k["name"]:
             continue
-        d = int(k["name"].split("paged_decode_tma_kernel<")[1].split(",")[1])
-        assert k["registers"] * threads[d] * ctas[d] <= 65536, k
+        args = [a.strip() for a in k["name"].split("paged_decode_tma_kernel<")[1].split(">")[0].split(",")]
+        d, warps = int(args[1]), int(args[3])
+        assert k["registers"] * (warps + 1) * 32 * ctas[d] <= 65536, k
