@@ -25,7 +25,8 @@ number of this library's kernel launches in the timed region, and:
   from its source for sm_100a) timed on the same device tensors the way the
   reference's benchmark times (10 warm-up calls, 100 calls each after a
   256 MB L2 flush, median), beside this library timed the same way, for the
-  headline workload and for c2, c3, c4 and their e4m3 variants;
+  headline workload and for c2, c3, c4 and their e4m3 variants, and
+  FlashInfer's batch decode (the reference benchmark's baseline) on c2-c4;
 * ``gather_parity`` (N>1): every head of the gathered output (head sharding)
   or of the merged output (sequence sharding) on every rank checked against
   the CPU oracle on sample sequences.
@@ -886,7 +887,7 @@ def run_gpu_arm(args) -> None:
         if names:
             del ws, out, q, kv, batch, outs, d_stage, ins  # the headline batch is no longer needed
             torch.cuda.empty_cache()
-            also = _also(names, max(args.steps, 100), args.warmup, dev, _peaks(), args.flashinfer)
+            also = _also(names, max(args.steps, 100), args.warmup, dev, _peaks(), not args.no_flashinfer)
 
     if rank == 0:
         step_s = device_s / args.steps
@@ -962,9 +963,8 @@ def main() -> None:
                     help="N=1: other workloads timed after the headline (comma-separated; empty for none)")
     ap.add_argument("--no-also", action="store_true",
                     help="skip the reference-kernel comparison and the other workloads")
-    ap.add_argument("--flashinfer", action="store_true",
-                    help="N=1: also time FlashInfer's batch decode on the 16-bit workloads under --also (it may "
-                         "compile kernels on first use)")
+    ap.add_argument("--no-flashinfer", action="store_true",
+                    help="N=1: skip FlashInfer's batch decode on the 16-bit workloads under --also")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
