@@ -177,6 +177,7 @@ class DkPlan(ctypes.Structure):
         ("smem_bytes", ctypes.c_int32),
         ("launches", ctypes.c_int32),
         ("ctas_per_sm", ctypes.c_int32),
+        ("fit_min_partition", ctypes.c_int32),
     ]
 
     def as_dict(self) -> dict:

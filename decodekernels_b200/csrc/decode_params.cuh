@@ -1,6 +1,7 @@
 // Parameters shared by the partition kernels and the merge kernel.
 #pragma once
 
+#include <limits.h>
 #include <stdint.h>
 
 namespace dkb {
@@ -53,6 +54,14 @@ struct DecodeParams {
   int kv_fp8;          // 1: the caches hold e4m3 bytes
   int compact;         // 1: live work items numbered densely (compact_coords); CTA b runs items b, b + G, ...
   int persistent;      // 1 (with compact): the grid is one wave of resident CTAs
+  // Partition size chosen on the device (fit_partition_size) when fit_slots > 0:
+  // a multiple of fit_gran tokens in [fit_min_partition, partition_size].
+  int fit_slots;          // resident CTAs of one wave of the partition kernel; 0: partition_size as planned
+  int fit_min_partition;  // smallest size the workspace rows allow (num_partitions >= ceil(max_seq_len / it))
+  int fit_gran;           // tokens: whole tiles of the partition kernel
+  // (With a fitted size the workspace's last row of (sequence 0, query head
+  // 0), which no partition reaches, carries the chosen size to the merge
+  // kernel: fit_size_slot.)
   // Head all-gather fused into the output stores (dk_paged_attention_decode_gather):
   // with peer_world > 0 every output row goes, instead of to `out`, to slot
   // (call parity) of every rank's receive buffer [2][num_seqs, peer_q_heads, D]
@@ -98,20 +107,29 @@ constexpr int kCompactPerLane = kCompactMaxSeqs / 32;
 // batch, a warp scan of the lanes' item counts finds the owner lane by
 // ballot, and the owner walks its sequences.  Also returns the item's
 // sequence length (clamped to [0, max_seq_len]).  False past the last item.
-__device__ __forceinline__ bool compact_coords(const DecodeParams& p, unsigned target, int lane, int& part,
-                                               int& kv_head, int& seq, int& seq_len) {
+// `partition_size` is the size in force for this launch (p.partition_size, or
+// fit_partition_size's choice).  STAGED: the lengths come from `staged`, the
+// clamped copy fit_partition_size left in shared memory, else from
+// p.seq_lens (one kind of load per instance, none issued speculatively).
+template <bool STAGED = false>
+__device__ __forceinline__ bool compact_coords(const DecodeParams& p, const int* staged, unsigned target, int lane,
+                                               int partition_size, int& part, int& kv_head, int& seq, int& seq_len) {
   const int per = (p.num_seqs + 31) >> 5;  // <= kCompactPerLane
   const int first = lane * per;
-  const unsigned ps = static_cast<unsigned>(p.partition_size);
+  const unsigned ps = static_cast<unsigned>(partition_size);
   const unsigned hkv = static_cast<unsigned>(p.num_kv_heads);
   int len[kCompactPerLane];
 #pragma unroll
   for (int j = 0; j < kCompactPerLane; ++j)
-    len[j] = j < per && first + j < p.num_seqs ? max(min(__ldg(p.seq_lens + first + j), p.max_seq_len), 0) : -1;
+    len[j] = j < per && first + j < p.num_seqs
+                 ? max(min(STAGED ? staged[first + j] : __ldg(p.seq_lens + first + j), p.max_seq_len), 0)
+                 : -1;
   unsigned parts[kCompactPerLane];
   unsigned mine = 0;
 #pragma unroll
   for (int j = 0; j < kCompactPerLane; ++j) {
+    parts[j] = 0;
+    if (j >= per) continue;  // warp-uniform: no lane has a sequence here, and no division runs for it
     parts[j] = len[j] < 0 ? 0u : 1u;  // an empty sequence keeps one item
     if (len[j] > static_cast<int>(ps)) parts[j] = (static_cast<unsigned>(len[j]) + ps - 1) / ps;
     mine += parts[j];
@@ -127,27 +145,130 @@ __device__ __forceinline__ bool compact_coords(const DecodeParams& p, unsigned t
   const int owner = __ffs(__ballot_sync(0xffffffffu, incl > target)) - 1;
   int f_seq = 0, f_head = 0, f_part = 0, f_len = 0;
   if (lane == owner) {
+    // walk to the item's sequence, then one division splits the remainder
     unsigned r = target - (incl - mine);
     bool found = false;
+    unsigned f_parts = 1;
 #pragma unroll
     for (int j = 0; j < kCompactPerLane; ++j) {
       const unsigned items = parts[j] * hkv;
       if (!found && r < items) {
         found = true;
         f_seq = first + j;
-        f_head = static_cast<int>(r / parts[j]);
-        f_part = static_cast<int>(r - static_cast<unsigned>(f_head) * parts[j]);
+        f_parts = parts[j];
         f_len = len[j];
       } else if (!found) {
         r -= items;
       }
     }
+    f_head = static_cast<int>(r / f_parts);
+    f_part = static_cast<int>(r - static_cast<unsigned>(f_head) * f_parts);
   }
   seq = __shfl_sync(0xffffffffu, f_seq, owner);
   kv_head = __shfl_sync(0xffffffffu, f_head, owner);
   part = __shfl_sync(0xffffffffu, f_part, owner);
   seq_len = __shfl_sync(0xffffffffu, f_len, owner);
   return true;
+}
+
+// Where the partition kernel leaves a fitted partition size for the merge
+// kernel (as float bits): exp_sums' last row of (sequence 0, query head 0).
+// The planner keeps that row out of every partition's reach.
+__device__ __forceinline__ float* fit_size_slot(const DecodeParams& p) {
+  return p.exp_sums + (p.ws_partitions - 1);
+}
+
+// Partition size fitted to the batch's lengths: the smallest multiple of
+// p.fit_gran in [p.fit_min_partition, p.partition_size] whose live items
+// (compact_coords' numbering) number at most p.fit_slots, so that every item
+// starts in the first wave of resident CTAs and the kernel takes about as
+// long as its longest partition; the planned p.partition_size when even its
+// items do not fit (its waves were sized for lengths near max_seq_len).  The
+// host sees only max_seq_len: a batch whose lengths sit far below it (a
+// lognormal spread, for example) leaves most of a wave idle at the planned
+// size.  FlashInfer's decode planner searches its KV chunk size for the same
+// bound, from host-side lengths; here the lengths stay on the device, so a
+// captured CUDA graph replays with the choice of each step's batch.
+//
+// All `nthreads` threads of the CTA call it (it holds __syncthreads).  The
+// clamped lengths go to shared memory once (`lens`, num_seqs ints; held in
+// registers instead, the read-only loads were re-issued for every candidate
+// under the partition kernel's register pressure); the partition kernel's
+// first compact_coords reads them from there too.  With t = ceil(L / gran)
+// per sequence, T = sum t over the N sequences and c = fit_slots / num_kv_heads,
+// the items at m tiles per partition, sum max(1, ceil(t / m)), lie in
+// [T / m, T / m + N]: no m < T / c fits, and every m >= T / (c - N) does, so
+// only sizes in [ceil(T / c), ceil(T / (c - N))] need counting (8 for e4m3
+// c4, against 20 in the workspace's range).  Warp w counts 4 of them at a
+// time, (m0 + 4w .. m0 + 4w + 3) * gran, then the next 4 * warps: lane l sums
+// max(1, ceil(t / m)) over sequences l, l + 32, ..., then one warp reduction
+// per candidate (the four chains are independent); `best` (shared) keeps
+// the smallest fitting candidate.  ceil(t / m) = umulhi(t + m - 1,
+// ceil(2^32 / m)), exact for (t + m - 1) * (m - 1) < 2^32: the planner fits
+// only max_seq_len <= 2^22 (t <= 2^16), and 2 <= m <= 2^10 here (sizes of
+// 512..2^16 tokens in tiles of 64 or 128, a power of two).  Every CTA of a
+// launch computes the same value; CTA 0 leaves it in fit_size_slot for the
+// merge kernel.
+__device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* lens, int* best, int tid, int nthreads) {
+  constexpr int K = 4;  // candidates per warp and round
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int warps = nthreads >> 5;
+  const int gran = p.fit_gran;
+  const int gran_log2 = __ffs(gran) - 1;
+  const int nj = (p.num_seqs + 31) >> 5;  // slots j holding a sequence in some lane (warp-uniform)
+  if (tid == 0) *best = INT_MAX;
+  for (int s = tid; s < p.num_seqs; s += nthreads) lens[s] = max(min(__ldg(p.seq_lens + s), p.max_seq_len), 0);
+  __syncthreads();
+  uint32_t tiles[kCompactPerLane];
+  unsigned total = 0;
+#pragma unroll
+  for (int j = 0; j < kCompactPerLane; ++j) {
+    tiles[j] = 0;
+    const int s = lane + 32 * j;
+    if (j < nj && s < p.num_seqs) {
+      tiles[j] = static_cast<uint32_t>((lens[s] + gran - 1) >> gran_log2);
+      total += tiles[j];
+    }
+  }
+  total = __reduce_add_sync(0xffffffffu, total);
+  const unsigned cap = static_cast<unsigned>(p.fit_slots / p.num_kv_heads);  // items per KV head
+  const unsigned nseq = static_cast<unsigned>(p.num_seqs);
+  const int hi = p.partition_size / gran;
+  const int lo = max(p.fit_min_partition / gran, cap > 0 ? static_cast<int>((total + cap - 1) / cap) : hi + 1);
+  int top = hi;  // the largest size that still needs counting
+  if (cap > nseq) top = max(lo, min(hi, static_cast<int>((total + cap - nseq - 1) / (cap - nseq))));
+#pragma unroll 1
+  for (int m0 = lo + K * warp; m0 <= top; m0 += K * warps) {
+    uint32_t magic[K];
+    unsigned n[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      magic[k] = 0xffffffffu / static_cast<uint32_t>(min(m0 + k, top)) + 1u;  // ceil(2^32 / m), m >= 2
+      n[k] = 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kCompactPerLane; ++j) {
+      if (j >= nj) break;
+      if (lane + 32 * j < p.num_seqs) {
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+          n[k] += max(1u, __umulhi(tiles[j] + static_cast<uint32_t>(min(m0 + k, top) - 1), magic[k]));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) n[k] = __reduce_add_sync(0xffffffffu, n[k]);
+    if (lane == 0) {
+      int fit = INT_MAX;
+#pragma unroll
+      for (int k = K - 1; k >= 0; --k)  // the smallest of the four that fits
+        if (m0 + k <= top && n[k] <= cap) fit = m0 + k;
+      if (fit != INT_MAX) atomicMin(best, fit);
+    }
+  }
+  __syncthreads();
+  const int b = *best;
+  return b == INT_MAX ? p.partition_size : b * gran;
 }
 
 }  // namespace dkb

@@ -1,7 +1,9 @@
 // Log-sum-exp merge of split-K partitions (DecodeKernels'
 // paged_attention_reduce_kernel, csrc/paged_attention.cuh:227-269):
 //   M = max_i m_i,  w_i = s_i exp(m_i - M),  out = sum_i w_i o_i / sum_i w_i
-// over the live partitions num_parts = min(ceil(L / partition_size), P);
+// over the live partitions num_parts = min(ceil(L / partition_size), P), with
+// the partition size the partition kernel used (fit_partition_size's choice
+// when the planner left it to the device);
 // zeros when L <= 0.  Sequences with a single live partition were already
 // written to `out` by the partition kernel and are skipped here.
 //
@@ -98,13 +100,16 @@ __global__ void __launch_bounds__(kMergeThreads) merge_partitions_kernel(const D
   const int q_head = blockIdx.x;
   const int seq = blockIdx.y;
   pdl_wait_primary();
+  // A fitted size: the partition kernel's choice, which its CTA 0 left in the
+  // reserved workspace slot (fit_size_slot).
+  const int ps = p.fit_slots > 0 ? __float_as_int(__ldcg(fit_size_slot(p))) : p.partition_size;
   const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
   if (seq_len <= 0) {
     for (int d = threadIdx.x * 4; d < D; d += kMergeThreads * 4)
       store_out4<T, D>(p, seq, q_head, d, make_float4(0.0f, 0.0f, 0.0f, 0.0f), -INFINITY);
     return;
   }
-  const int num_parts = min((seq_len + p.partition_size - 1) / p.partition_size, p.num_partitions);
+  const int num_parts = min((seq_len + ps - 1) / ps, p.num_partitions);
   if (num_parts <= 1) return;  // written by the partition kernel
   merge_rows<T, D>(p, seq, q_head, num_parts);
 }

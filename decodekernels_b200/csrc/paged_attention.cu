@@ -29,9 +29,11 @@
 namespace dkb {
 namespace {
 
-constexpr int kVersion = 700;  // 0.7.0: dk_gather_heads, DK_FLAG_PERSISTENT; 0.6.0: dk_exchange_merge_lse; 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale / v_scale); 0.4.0:
-                                // dk_paged_attention_decode_lse / dk_merge_lse; 0.3.0: dk_reshape_and_cache;
-                                // 0.2.0: DkPagedAttnArgs.merge_counters
+// 0.8.0: DkPlan.fit_min_partition (partition size fitted on the device); 0.7.0: dk_gather_heads,
+// DK_FLAG_PERSISTENT; 0.6.0: dk_exchange_merge_lse; 0.5.0: e4m3 caches (DkPagedAttnArgs.kv_fp8 / k_scale /
+// v_scale); 0.4.0: dk_paged_attention_decode_lse / dk_merge_lse; 0.3.0: dk_reshape_and_cache; 0.2.0:
+// DkPagedAttnArgs.merge_counters
+constexpr int kVersion = 800;
 // Planner: partitions are sized so that the grid is about one wave of
 // kPlanCtasPerSm CTAs per SM if every sequence had max_seq_len tokens, within
 // at least kMinPartition tokens (overridable for tuning sweeps).
@@ -121,8 +123,12 @@ constexpr int tma_stages() {
 #ifndef DK_TMA_FP8_WARPS_D256
 #define DK_TMA_FP8_WARPS_D256 DK_TMA_WARPS_D256
 #endif
+// e4m3 head_dim 128: three CTAs of its 65 KB ring fit an SM, and the bound
+// lets the registers follow (117-120 each, no spill; without it ptxas chose
+// 96 and the compact instance spilled).  c3f8 45.2 -> 44.0 us, c2f8 57.5 ->
+// 57.0 us.
 #ifndef DK_TMA_FP8_MIN_CTAS_D128
-#define DK_TMA_FP8_MIN_CTAS_D128 0
+#define DK_TMA_FP8_MIN_CTAS_D128 3
 #endif
 #ifndef DK_TMA_FP8_MIN_CTAS_D256
 #define DK_TMA_FP8_MIN_CTAS_D256 0
@@ -285,6 +291,30 @@ constexpr long long kVariedBytes = DK_PLAN_VARIED_BYTES;
 #endif
 constexpr int kVariedWaves = DK_PLAN_VARIED_WAVES;
 constexpr long long kMaxBytes = DK_PLAN_MAX_BYTES;
+// Partition size fitted on the device (fit_partition_size), for e4m3
+// caches in batches of 2..kCompactMaxSeqs sequences with at most one
+// (sequence, KV head) pair per SM: the planner's size (waves sized as if
+// every sequence had max_seq_len tokens) is only an upper bound, and the
+// partition kernel picks the smallest size down to kFitMinPartition tokens
+// -- the reference's fixed partition size, so a workspace sized as its
+// wrapper sizes it allows nearly the full range -- whose live items fit one
+// wave.  An e4m3 CTA's time follows its tokens (its consumers' math is the
+// limit), so a wave left idle by lengths spread far below max_seq_len is
+// lost time: e4m3 c4 (MQA, lognormal lengths) has 323 items for 444
+// resident CTAs at the planned 1728 tokens, 55.0 us, and 429 items at the
+// fitted 1216, 47.2 us with the size fixed.  A 16-bit CTA shares HBM with
+// the others, and c4 ran 76.5 us at 1728 against 77.5 at 1216: no fit.
+#ifndef DK_FIT_MIN_PARTITION
+#define DK_FIT_MIN_PARTITION 512
+#endif
+constexpr int kFitMinPartition = DK_FIT_MIN_PARTITION;
+
+bool fit_shape(int num_seqs, int num_kv_heads, int max_seq_len, int sms) {
+  const long long pairs = static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1);
+  // (max_seq_len <= 2^22 keeps fit_partition_size's fp32 ceil-division exact)
+  return num_seqs > 1 && num_seqs <= kCompactMaxSeqs && pairs <= sms && max_seq_len > kFitMinPartition &&
+         max_seq_len <= (1 << 22);
+}
 
 int desired_partition_size(int num_seqs, int num_kv_heads, int head_dim, int max_seq_len, int sms, int kv_bytes = 2) {
   const long long pairs = std::max<long long>(1, static_cast<long long>(num_seqs) * std::max(num_kv_heads, 1));
@@ -355,6 +385,7 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   pl->path = tma_eligible(a) ? DK_PATH_TMA_MMA : DK_PATH_SIMT;
   const int L = a.max_seq_len;
   int ps, parts;
+  int fit_parts = 0;  // partitions at the planned size when the device fits it
   if (L <= 0) {
     ps = DK_TILE_TOKENS;
     parts = 1;
@@ -373,6 +404,19 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
       ps = round_up(ceil_div(L, a.max_partitions), gran);
       parts = ceil_div(L, ps);
     }
+    if (a.partition_size <= 0 && pl->path == DK_PATH_TMA_MMA && a.kv_fp8 && a.max_partitions >= 2 &&
+        fit_shape(a.num_seqs, a.num_kv_heads, L, num_sms(dev))) {
+      // ps becomes the upper bound of the device's choice.  The rows cover
+      // the smallest size the workspace allows plus one: the last row of
+      // (sequence 0, query head 0) passes the chosen size to the merge
+      // kernel (fit_size_slot), and no partition reaches it.
+      const int lo = std::max(round_up(kFitMinPartition, gran), round_up(ceil_div(L, a.max_partitions - 1), gran));
+      if (lo < ps) {
+        pl->fit_min_partition = lo;
+        fit_parts = parts;
+        parts = ceil_div(L, lo) + 1;
+      }
+    }
   }
   pl->partition_size = ps;
   pl->num_partitions = parts;
@@ -390,7 +434,10 @@ void make_plan(const DkPagedAttnArgs& a, int dev, DkPlan* pl) {
   // c2 105.7 -> 103-105, c5 and a rank's share of c5 at 2 / 4 / 8 GPUs
   // 0.2-0.4% faster); large merges are faster with the separate kernel
   // (c3 86 vs 90.5 us, c4 83 vs 90 us).
-  const long long merge_bytes = 1LL * parts * (a.num_q_heads / a.num_kv_heads) * (a.head_dim + 2) * 4;
+  // (A fitted size counts at its upper bound: the device never picks
+  // more partitions than fit one wave.)
+  const long long merge_bytes =
+      1LL * (fit_parts > 0 ? fit_parts : parts) * (a.num_q_heads / a.num_kv_heads) * (a.head_dim + 2) * 4;
   const bool small = merge_bytes <= kFusedMergeMaxBytes;
   const bool fused = pl->split && a.merge_counters != nullptr && (small || (a.flags & DK_FLAG_FORCE_FUSED_MERGE));
   pl->launches = pl->split && !fused ? 2 : 1;
@@ -554,25 +601,32 @@ int occupancy_of(Kernel kernel, int threads, int smem, int dev, bool* attr_done)
   return n;
 }
 
-template <typename T, int D>
-int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
-  if (pl.path == DK_PATH_TMA_MMA && fp8) {
+template <typename T, int D, bool COMPACT>
+int tma_occupancy(bool fp8, int dev) {
+  if (fp8) {
     if constexpr (D >= 128) {
       using Shape = TmaShapeFp8<D>;
       static bool attr_done[kMaxDevices] = {false};
-      return occupancy_of(paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices, Shape::kMinCtas>,
-                          Shape::Cfg::kThreads,
-                          Shape::Cfg::kSmemBytes, dev, attr_done);
+      return occupancy_of(
+          paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, true, Shape::kSlices, Shape::kMinCtas, COMPACT>,
+          Shape::Cfg::kThreads, Shape::Cfg::kSmemBytes, dev, attr_done);
     }
     return 0;
   }
-  if (pl.path == DK_PATH_TMA_MMA) {  // the dense-grid instance launch_tma runs
-    using Shape = TmaShape<D>;
-    static bool attr_done[kMaxDevices] = {false};
-    return occupancy_of(
-        paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, false, Shape::kSlices, Shape::kMinCtas>,
-        Shape::Cfg::kThreads, Shape::Cfg::kSmemBytes, dev, attr_done);
-  }
+  using Shape = TmaShape<D>;
+  static bool attr_done[kMaxDevices] = {false};
+  return occupancy_of(
+      paged_decode_tma_kernel<T, D, Shape::kStages, Shape::kWarps, false, Shape::kSlices, Shape::kMinCtas, COMPACT>,
+      Shape::Cfg::kThreads, Shape::Cfg::kSmemBytes, dev, attr_done);
+}
+
+// Resident CTAs per SM of the partition kernel instance the plan runs (for a
+// fitted partition size, the compact-grid instance whose one wave the device
+// fills).
+template <typename T, int D>
+int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
+  if (pl.path == DK_PATH_TMA_MMA)
+    return pl.fit_min_partition > 0 ? tma_occupancy<T, D, true>(fp8, dev) : tma_occupancy<T, D, false>(fp8, dev);
   static bool attr_done[kMaxDevices] = {false};
   return fp8 ? occupancy_of(paged_decode_simt_kernel<T, D, uint8_t>, kSimtThreads, SimtConfig<D>::kSmemBytes, dev,
                             attr_done)
@@ -628,8 +682,15 @@ int launch_tma(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int 
   if (e != cudaSuccess)
     return fail_cuda(e, FP8 ? "cudaFuncSetAttribute(fp8 partition kernel)" : "cudaFuncSetAttribute(partition kernel)");
   dim3 grid(static_cast<unsigned>(pl.num_ctas));
-  if (COMPACT)
-    grid.x = compact_grid(kernel, Shape::Cfg::kThreads, smem, dev, pl.num_ctas, p.persistent ? 1 : kCompactWaves, occ);
+  if (COMPACT) {
+    // A fitted partition size puts every item in one wave when the lengths
+    // allow it, and one wave of CTAs runs them; the CTAs loop over the items
+    // when they do not.
+    const bool fit = pl.fit_min_partition > 0;
+    grid.x = compact_grid(kernel, Shape::Cfg::kThreads, smem, dev, pl.num_ctas, p.persistent || fit ? 1 : kCompactWaves,
+                          occ);
+    if (fit && dev >= 0 && dev < kMaxDevices && occ[dev] > 0) p.fit_slots = occ[dev] * num_sms(dev);
+  }
   CUtensorMap kmap, vmap;
   if (int r = build_maps<D>(a, p, dev, &kmap, &vmap)) return r;
   e = launch_pdl(kernel, grid, dim3(Shape::Cfg::kThreads), smem, stream, kmap, vmap, p);
@@ -727,10 +788,15 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   // scan of the lengths (one L2 round trip) before their first loads; that
   // is repaid where the consumers' math bounds a CTA (e4m3: c4 80.7 ->
   // ~73 us) but not where HBM does (16-bit c4: 85 -> 89 us).
+  // And whenever the device fits the partition size (fit_partition_size).
   const bool persistent = (a.flags & DK_FLAG_PERSISTENT) != 0;
   p.compact = pl.path == DK_PATH_TMA_MMA && a.num_seqs <= kCompactMaxSeqs &&
-              (persistent || (a.kv_fp8 && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1));
+              (persistent || pl.fit_min_partition > 0 ||
+               (a.kv_fp8 && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1));
   p.persistent = p.compact && persistent;
+  p.fit_min_partition = pl.fit_min_partition;
+  p.fit_gran = pl.path == DK_PATH_TMA_MMA && a.kv_fp8 ? tma_tile_fp8(a.head_dim) : DK_TILE_TOKENS;
+  p.fit_slots = 0;  // set at launch from the kernel's occupancy
   p.scale_log2 = a.scale * (a.kv_fp8 ? a.k_scale : 1.0f) * kLog2e;
   p.v_scale = a.kv_fp8 ? a.v_scale : 1.0f;
   if (peer != nullptr) {
@@ -1056,6 +1122,16 @@ int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t s
   a.merge_counters = nullptr;
   DkPlan pl;
   dkb::make_plan(a, dev, &pl);
+  const size_t row_bytes = static_cast<size_t>(a.num_seqs) * a.num_q_heads * (a.head_dim + 2) * sizeof(float);
+  if (pl.fit_min_partition > 0 && row_bytes * pl.num_partitions > DK_NOALLOC_SCRATCH_BYTES) {
+    // A fitted size's rows (down to its floor) do not fit the scratch, the
+    // planned size's do: raise the floor to what the scratch holds.
+    const size_t fit_rows = DK_NOALLOC_SCRATCH_BYTES / row_bytes;
+    if (fit_rows >= static_cast<size_t>(dkb::ceil_div(a.max_seq_len, pl.partition_size))) {
+      a.max_partitions = static_cast<int>(fit_rows);
+      dkb::make_plan(a, dev, &pl);
+    }
+  }
   a.max_partitions = 0;
   if (pl.split) {
     const size_t rows = static_cast<size_t>(a.num_seqs) * a.num_q_heads * pl.num_partitions;
@@ -1076,10 +1152,10 @@ int dk_paged_attention_decode_noalloc(const DkPagedAttnArgs* args, dk_stream_t s
     const long long pairs = static_cast<long long>(a.num_seqs) * a.num_kv_heads;
     if (pairs <= dkb::kNoallocCounters) {
       a.merge_counters = counters;  // one launch when the merge is small
-      const int fixed = a.partition_size;
-      a.partition_size = pl.partition_size;  // same partitions; only the merge choice is re-planned
+      // Same partitions (the rows hold the planned count, so neither the
+      // planned size nor a fitted size's floor moves); only the merge choice
+      // is re-planned.
       dkb::make_plan(a, dev, &pl);
-      a.partition_size = fixed;
       if (pl.launches == 1) {
         // Start from zero whatever an earlier call left behind (a wait that
         // gave up leaves its pairs' counts part-way); a memset allocates nothing.
@@ -1120,7 +1196,13 @@ int32_t dk_num_partitions(int32_t num_seqs, int32_t num_kv_heads, int32_t head_d
     dev = -1;
   }
   const int hkv = num_kv_heads <= 0 ? 1 : num_kv_heads;
-  const int ps = dkb::desired_partition_size(num_seqs, hkv, head_dim, max_seq_len, dkb::num_sms(dev));
+  const int sms = dkb::num_sms(dev);
+  const int ps = dkb::desired_partition_size(num_seqs, hkv, head_dim, max_seq_len, sms);
+  // rows down to the smallest size the device may fit, plus the row that
+  // passes its choice to the merge kernel (the cache type and path are not
+  // known here)
+  if (dkb::fit_shape(num_seqs, hkv, max_seq_len, sms) && ps > dkb::kFitMinPartition)
+    return dkb::ceil_div(max_seq_len, dkb::kFitMinPartition) + 1;
   return dkb::ceil_div(max_seq_len, ps);
 }
 

@@ -223,17 +223,19 @@ __device__ __forceinline__ void merge_if_last(const DecodeParams& p, int seq, in
   }
 }
 
-// Result of partition `part` of the partition kernels.  A
-// sequence whose whole length fits in partition 0 needs no merge: its result
-// also goes straight to `out` (the merge kernel skips it), while the
-// workspace row is still written so the workspace keeps the same contents.
+// Result of partition `part` (of `partition_size` tokens, the size in force
+// for this launch) of the partition kernels.  A sequence whose whole length
+// fits in partition 0 needs no merge: its result also goes straight to `out`
+// (the merge kernel skips it), while the workspace row is still written so
+// the workspace keeps the same contents.
 template <typename T, int D, int WARPS, typename Sync>
 __device__ __forceinline__ void write_partition_result(const DecodeParams& p, float* red, int seq, int kv_head,
-                                                       int part, int seq_len, int tid, int nthreads, Sync sync) {
-  const bool to_out = !p.split || (part == 0 && seq_len <= p.partition_size);
+                                                       int part, int seq_len, int partition_size, int tid,
+                                                       int nthreads, Sync sync) {
+  const bool to_out = !p.split || (part == 0 && seq_len <= partition_size);
   write_merged_result<T, D, WARPS>(p, red, seq, kv_head, part, p.split != 0, to_out, tid, nthreads, sync);
   if (p.merge_counters != nullptr && !to_out)
-    merge_if_last<T, D>(p, seq, kv_head, (seq_len + p.partition_size - 1) / p.partition_size, tid, nthreads, sync);
+    merge_if_last<T, D>(p, seq, kv_head, (seq_len + partition_size - 1) / partition_size, tid, nthreads, sync);
 }
 
 // Empty sequences get exact zeros from the partition kernel when no merge

@@ -142,8 +142,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     }
   }
   __syncthreads();
-  write_partition_result<T, D, WARPS>(p, simt_smem, seq, kv_head, part, seq_len, threadIdx.x, kSimtThreads,
-                                      [] { __syncthreads(); });
+  write_partition_result<T, D, WARPS>(p, simt_smem, seq, kv_head, part, seq_len, p.partition_size, threadIdx.x,
+                                      kSimtThreads, [] { __syncthreads(); });
 }
 
 }  // namespace dkb

@@ -84,6 +84,8 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
   __shared__ __align__(8) uint64_t full_bar[NSTAGES];
   __shared__ __align__(8) uint64_t empty_bar[NSTAGES];
   __shared__ int s_item[4];  // compact grid: seq (-1: no item), kv_head, partition, length
+  __shared__ int s_fit;      // compact grid: fit_partition_size's smallest fitting candidate
+  __shared__ int s_ps;       // compact grid: the partition size in force
   __shared__ int s_abort;    // compact grid: a bounded wait gave up, so run no further item
 
   int part = 0, kv_head = 0, seq = 0;
@@ -124,13 +126,22 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
   const bool box_lane = warp == WARPS && (lane < PAGES || v_lane);
   const int bs_log2 = p.bs_log2;
   const int bs_mask = (1 << bs_log2) - 1;
+  // The partition size in force: p.partition_size, or on the compact grid
+  // fit_partition_size's choice when p.fit_slots > 0.  Read where it is used
+  // (per item, not in the tile loop) so that it holds no register across it.
+  auto part_size = [&]() -> int {
+    if constexpr (COMPACT)
+      return *static_cast<volatile int*>(&s_ps);
+    else
+      return p.partition_size;
+  };
   float* red = reinterpret_cast<float*>(smem);  // merge scratch, over the ring once an item's tiles are read
 
   // The tiles of one item (pstart < seq_len) and its result; g0 = tiles this
   // CTA ran before it (ring position and barrier phases).
   auto run_item = [&](int part, int kv_head, int seq, int seq_len, int pb, int off, uint32_t g0) {
-    const int pstart = part * p.partition_size;
-    const int pend = min(pstart + p.partition_size, seq_len);
+    const int pstart = part * part_size();
+    const int pend = min(pstart + part_size(), seq_len);
     const int ntiles = (pend - pstart + TILE - 1) / TILE;
     if (warp == WARPS) {
       // ------------------------------------------------------------------ producer
@@ -164,8 +175,8 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
       // The producer then helps with the merge (it holds no partial state).
       named_bar_sync(1, Cfg::kThreads);
       named_bar_sync(1, Cfg::kThreads);
-      write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
-                                          [] { named_bar_sync(1, Cfg::kThreads); });
+      write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, part_size(), threadIdx.x,
+                                          Cfg::kThreads, [] { named_bar_sync(1, Cfg::kThreads); });
       return;
     }
     // -------------------------------------------------------------------- consumers
@@ -206,8 +217,8 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     named_bar_sync(1, Cfg::kThreads);
     wa.to_red(red, WARPS, warp, p.group, lane);
     named_bar_sync(1, Cfg::kThreads);
-    write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, threadIdx.x, Cfg::kThreads,
-                                        [] { named_bar_sync(1, Cfg::kThreads); });
+    write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, part_size(), threadIdx.x,
+                                        Cfg::kThreads, [] { named_bar_sync(1, Cfg::kThreads); });
     if constexpr (COMPACT) {
       // A warp with no rows in the last tile arrives on its empty barrier now,
       // when every warp has finished reading the ring (the epilogue's
@@ -219,7 +230,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
 
   // The block ids of an item's first tile (producer lanes).
   auto first_page = [&](int part, int seq, int& pb, int& off) {
-    const int tok = part * p.partition_size + (kslot << rows_log2);
+    const int tok = part * part_size() + (kslot << rows_log2);
     if (box_lane && tok < p.max_seq_len) {
       pb = __ldg(p.block_tables + static_cast<int64_t>(seq) * p.bt_stride + (tok >> bs_log2));
       off = tok & bs_mask;
@@ -239,11 +250,39 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     }
     run_item(part, kv_head, seq, seq_len, pb, off, 0u);
   } else {
+    // With a fitted size (e4m3 caches only: the 16-bit instances carry no
+    // fit code) the first item's coordinates read the lengths that
+    // fit_partition_size staged at the start of the ring (inputs of this
+    // call, readable after the grid-dependency wait above).
+    bool from_ring = false;
+    if (FP8 && p.fit_slots > 0) {
+      const int ps = fit_partition_size(p, reinterpret_cast<int*>(smem), &s_fit, threadIdx.x, Cfg::kThreads);
+      from_ring = true;
+      if (threadIdx.x == 0) {
+        s_ps = ps;
+        if (blockIdx.x == 0 && p.split) *fit_size_slot(p) = __int_as_float(ps);  // for the merge kernel
+      }
+    } else if (threadIdx.x == 0) {
+      s_ps = p.partition_size;
+    }
+    __syncthreads();
     uint32_t g0 = 0;
     for (unsigned item = blockIdx.x;; item += gridDim.x) {
       if (warp == 0) {
         int len = 0;
-        const bool live = compact_coords(p, item, lane, part, kv_head, seq, len);
+        bool live;
+        if constexpr (FP8) {
+          const int* staged = reinterpret_cast<const int*>(smem);
+          live = from_ring ? compact_coords<true>(p, staged, item, lane, part_size(), part, kv_head, seq, len)
+                           : compact_coords(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
+        } else {
+          live = compact_coords(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
+        }
+        if (from_ring) {
+          // the ring's first TMA writes follow: order these reads of it before them
+          fence_proxy_async_smem();
+          from_ring = false;
+        }
         if (lane == 0) {
           s_item[0] = live ? seq : -1;
           s_item[1] = kv_head;
@@ -257,7 +296,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
       kv_head = s_item[1];
       part = s_item[2];
       const int seq_len = s_item[3];
-      const int pstart = part * p.partition_size;
+      const int pstart = part * part_size();
       if (pstart >= seq_len) {
         // an empty sequence's item
         if (partition_writes_zeros(p, part, seq_len)) write_zero_output<T, D>(p, seq, kv_head, threadIdx.x, Cfg::kThreads);
@@ -265,7 +304,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
         int pb = 0, off = 0;
         first_page(part, seq, pb, off);
         run_item(part, kv_head, seq, seq_len, pb, off, g0);
-        g0 += (min(pstart + p.partition_size, seq_len) - pstart + TILE - 1) / TILE;
+        g0 += (min(pstart + part_size(), seq_len) - pstart + TILE - 1) / TILE;
       }
       // The next item's TMA writes reuse the ring that the merge scratch
       // occupied: order those generic accesses before them, and keep s_item

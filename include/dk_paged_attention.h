@@ -135,6 +135,10 @@ typedef struct DkPlan {
   int32_t smem_bytes;     /* dynamic shared memory of the partition kernel */
   int32_t launches;       /* kernels launched by one call (1 or 2; 1 with merge counters) */
   int32_t ctas_per_sm;    /* resident partition-kernel CTAs per SM (occupancy query; 0 without a GPU) */
+  int32_t fit_min_partition; /* > 0: partition_size is an upper bound; each launch fits the size on the
+                                device to the batch's lengths (the smallest multiple of the kernel's tile,
+                                down to this, whose live items fit one wave of resident CTAs), and
+                                num_partitions covers this smallest size.  0: partition_size is used. */
 } DkPlan;
 
 /*

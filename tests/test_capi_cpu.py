@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     out = subprocess.run(["nm", "-D", "--defined-only", str(capi.LIB_PATH)], capture_output=True, text=True).stdout
     exported = set(re.findall(r" T (dk_\w+)", out))
     assert set(_declared()) <= exported
-    assert capi.version() == 700
+    assert capi.version() == 800
 
 
 def test_struct_layout_matches_header(tmp_path):
@@ -40,7 +40,7 @@ def test_struct_layout_matches_header(tmp_path):
     include/dk_paged_attention.h."""
     # 10 pointers + 11 int64 + 12 int32 + 3 float = 228 bytes, padded to 232 (8-byte alignment)
     assert ctypes.sizeof(capi.DkPagedAttnArgs) == 232
-    assert ctypes.sizeof(capi.DkPlan) == 36
+    assert ctypes.sizeof(capi.DkPlan) == 40
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "dk_paged_attention.h"', "int main(void) {"]
     structs = (("DkPagedAttnArgs", capi.DkPagedAttnArgs), ("DkPlan", capi.DkPlan),
                ("DkCacheWriteArgs", capi.DkCacheWriteArgs), ("DkLseMergeArgs", capi.DkLseMergeArgs),
@@ -248,8 +248,45 @@ def _wide_ws(n, hq, parts, d):
 def test_planner_partition_sizes(n, hq, hkv, d, bs, L, want):
     """The planner's choices for the measured shapes (148 SMs assumed without
     a GPU): few pairs get partitions for ~8 waves of CTAs, within
-    [512 KB, 2 MB] of 16-bit K+V."""
+    [512 KB, 2 MB] of 16-bit K+V.  16-bit caches never fit the size on the
+    device."""
     rc, p = _plan(_args(n=n, hq=hq, hkv=hkv, d=d, bs=bs, max_seq_len=L, ws=_wide_ws(n, hq, -(-L // 64), d)))
     assert rc == 0, capi.last_error()
-    assert p["partition_size"] == want
+    assert p["partition_size"] == want and p["fit_min_partition"] == 0
     assert p["num_partitions"] == -(-L // want)
+    assert capi.num_partitions(n, hkv, d, bs, L) >= p["num_partitions"]
+
+
+def _fp8_plan(n, hq, hkv, d, bs, L, rows, partition_size=0):
+    kv8 = torch.zeros(64, bs, hkv, d, dtype=torch.uint8)
+    q = torch.zeros(n, hq, d, dtype=torch.bfloat16)
+    bt = torch.zeros(n, 64, dtype=torch.int32)
+    sl = torch.zeros(n, dtype=torch.int32)
+    a = capi.make_args(q, kv8, kv8, bt, sl, d**-0.5, L, q, _wide_ws(n, hq, rows, d), partition_size, False, 0, 0.5,
+                       0.5)
+    return _plan(a)
+
+
+def test_fitted_partition_floor_follows_the_workspace():
+    """e4m3 c4's shape: the planned 1728 tokens bound the device's fit, down
+    to 512 with the workspace the library sizes (its rows: down to 512 tokens,
+    plus the row passing the choice to the merge kernel).  Fewer rows raise
+    the floor (the last row stays out of the partitions' reach); too few for
+    any fit leave the planned size fixed; a size the caller fixes is never
+    fitted; neither is a lone sequence, nor a batch with more (sequence, KV
+    head) pairs than SMs."""
+    n, hq, hkv, d, bs, L = 128, 8, 1, 256, 32, 32768
+    rows = capi.num_partitions(n, hkv, d, bs, L)
+    assert rows == L // 512 + 1
+    rc, p = _fp8_plan(n, hq, hkv, d, bs, L, rows)
+    assert rc == 0 and p["partition_size"] == 1728 and p["fit_min_partition"] == 512 and p["num_partitions"] == rows
+    rc, p = _fp8_plan(n, hq, hkv, d, bs, L, 32)
+    assert rc == 0 and p["fit_min_partition"] == 1088 and p["num_partitions"] == 32 and p["partition_size"] == 1728
+    rc, p = _fp8_plan(n, hq, hkv, d, bs, L, 19)
+    assert rc == 0 and p["fit_min_partition"] == 0 and p["num_partitions"] == 19
+    rc, p = _fp8_plan(n, hq, hkv, d, bs, L, rows, partition_size=1024)
+    assert rc == 0 and p["fit_min_partition"] == 0 and p["partition_size"] == 1024
+    rc, p = _fp8_plan(1, 64, 8, 128, 16, 131072, 2048)
+    assert rc == 0 and p["fit_min_partition"] == 0
+    rc, p = _fp8_plan(160, 8, 1, 256, 32, L, rows)
+    assert rc == 0 and p["fit_min_partition"] == 0
