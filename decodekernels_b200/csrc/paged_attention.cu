@@ -781,19 +781,24 @@ int launch(const DkPagedAttnArgs& a, const DkPlan& pl, int dev, cudaStream_t str
   p.split = pl.split;
   p.kv_fp8 = a.kv_fp8;
   // Compact grid (compact_coords) when most CTAs of the dense grid may have no
-  // tokens: many partitions per sequence, and few enough sequences that every
-  // CTA's warp scan of the lengths stays short.
-  // Compact grid (compact_coords): with DK_FLAG_PERSISTENT, and by default
-  // for e4m3 caches when a sequence may span many partitions.  Its CTAs pay a
-  // scan of the lengths (one L2 round trip) before their first loads; that
-  // is repaid where the consumers' math bounds a CTA (e4m3: c4 80.7 ->
-  // ~73 us) but not where HBM does (16-bit c4: 85 -> 89 us).
-  // And whenever the device fits the partition size (fit_partition_size).
+  // tokens -- a sequence may span many partitions -- and few enough sequences
+  // that every CTA's warp scan of the lengths stays short; its CTAs pay that
+  // scan before their first loads.  With DK_FLAG_PERSISTENT, whenever the
+  // device fits the partition size (fit_partition_size), and by default:
+  // * e4m3 caches, 4 waves of CTAs: the consumers' math bounds a CTA (c4f8
+  //   80.7 -> ~73 us with the planned size);
+  // * 16-bit caches with at most one (sequence, KV head) pair per SM, one
+  //   wave (the persistent grid): c4 78.2 -> 76.5 us at the planned 1728
+  //   tokens, where the dense grid's 2432 CTAs hold 323 live items.  (4 waves
+  //   measured slower on an earlier kernel, c4 85 -> 89 us; HBM bounds a
+  //   16-bit CTA, and the empty CTAs' dispatch is what the one wave saves.)
   const bool persistent = (a.flags & DK_FLAG_PERSISTENT) != 0;
+  const bool sparse = pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1;
+  const bool one_wave16 =
+      !a.kv_fp8 && sparse && fit_shape(a.num_seqs, a.num_kv_heads, a.max_seq_len, num_sms(dev));
   p.compact = pl.path == DK_PATH_TMA_MMA && a.num_seqs <= kCompactMaxSeqs &&
-              (persistent || pl.fit_min_partition > 0 ||
-               (a.kv_fp8 && pl.num_partitions >= kCompactMinPartitions && a.num_seqs > 1));
-  p.persistent = p.compact && persistent;
+              (persistent || pl.fit_min_partition > 0 || (a.kv_fp8 && sparse) || one_wave16);
+  p.persistent = p.compact && (persistent || one_wave16);
   p.fit_min_partition = pl.fit_min_partition;
   p.fit_gran = pl.path == DK_PATH_TMA_MMA && a.kv_fp8 ? tma_tile_fp8(a.head_dim) : DK_TILE_TOKENS;
   p.fit_slots = 0;  // set at launch from the kernel's occupancy
