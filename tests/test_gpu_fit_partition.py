@@ -40,8 +40,10 @@ def _lognormal_lens(n, seed, median=2048, sigma=1.0, zeros=()):
 
 
 def _gran(fp8, d):
-    """Tokens per tile of the partition kernel: the unit of a fitted size."""
-    return 128 if fp8 and d == 128 else 64
+    """Tokens per tile of the e4m3 partition kernel, the unit of a fitted
+    size: 4 consumer warps x two 16-token slices at head_dim 128, 2 warps x
+    one slice at 256."""
+    return 128 if d == 128 else 32
 
 
 def _predicted(lens, hkv, plan, gran):
