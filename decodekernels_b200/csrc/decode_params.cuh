@@ -198,15 +198,16 @@ __device__ __forceinline__ float* fit_size_slot(const DecodeParams& p) {
 // per sequence, T = sum t over the N sequences and c = fit_slots / num_kv_heads,
 // the items at m tiles per partition, sum max(1, ceil(t / m)), lie in
 // [T / m, T / m + N]: no m < T / c fits, and every m >= T / (c - N) does, so
-// only sizes in [ceil(T / c), ceil(T / (c - N))] need counting (8 for e4m3
-// c4, against 20 in the workspace's range).  Warp w counts 4 of them at a
+// only sizes in [ceil(T / c), ceil(T / (c - N))] need counting, within the
+// planned size (8 for e4m3 c4, against 39 in the workspace's range; none
+// when ceil(T / c) is above the planned size, which then stays).  Warp w counts 4 of them at a
 // time, (m0 + 4w .. m0 + 4w + 3) * gran, then the next 4 * warps: lane l sums
 // max(1, ceil(t / m)) over sequences l, l + 32, ..., then one warp reduction
 // per candidate (the four chains are independent); `best` (shared) keeps
 // the smallest fitting candidate.  ceil(t / m) = umulhi(t + m - 1,
 // ceil(2^32 / m)), exact for (t + m - 1) * (m - 1) < 2^32: the planner fits
-// only max_seq_len <= 2^22 (t <= 2^16), and 2 <= m <= 2^10 here (sizes of
-// 512..2^16 tokens in tiles of 64 or 128, a power of two).  Every CTA of a
+// only max_seq_len <= 2^22, and sizes of 512..8192 tokens in tiles of 32 to
+// 128 (a power of two), so t <= 2^17 and 4 <= m <= 2^8.  Every CTA of a
 // launch computes the same value; CTA 0 leaves it in fit_size_slot for the
 // merge kernel.
 __device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* lens, int* best, int tid, int nthreads) {
@@ -236,8 +237,8 @@ __device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* le
   const unsigned nseq = static_cast<unsigned>(p.num_seqs);
   const int hi = p.partition_size / gran;
   const int lo = max(p.fit_min_partition / gran, cap > 0 ? static_cast<int>((total + cap - 1) / cap) : hi + 1);
-  int top = hi;  // the largest size that still needs counting
-  if (cap > nseq) top = max(lo, min(hi, static_cast<int>((total + cap - nseq - 1) / (cap - nseq))));
+  int top = hi;  // the largest size that still needs counting (none when lo > hi)
+  if (cap > nseq) top = min(hi, max(lo, static_cast<int>((total + cap - nseq - 1) / (cap - nseq))));
 #pragma unroll 1
   for (int m0 = lo + K * warp; m0 <= top; m0 += K * warps) {
     uint32_t magic[K];

@@ -113,11 +113,15 @@ def test_sixteen_bit_caches_keep_the_planned_size():
     assert_attention_close(out, oracle_dense(q, kv), torch.bfloat16, "16-bit, planned size")
 
 
-def test_lengths_near_the_bound_keep_the_planned_size():
+@pytest.mark.parametrize("n,step", [(24, 37), (37, 0)])
+def test_lengths_near_the_bound_keep_the_planned_size(n, step):
     # every sequence near max_seq_len: the planned size's items exceed a wave,
-    # so the device keeps it (and the CTAs of one wave loop over the items)
-    n, hkv, group, d = 24, 2, 8, 128
-    lens = [MAX_LEN - 37 * i for i in range(n)]
+    # so the device keeps it (and the CTAs of one wave loop over the items).
+    # 37 sequences of 32768 tokens: some size above the planned one would fit
+    # the wave (43 tiles of 128 tokens, 222 items per KV head at 3 CTAs per
+    # SM), and the device must not pick it.
+    hkv, group, d = 2, 8, 128
+    lens = [MAX_LEN - step * i for i in range(n)]
     kv = make_paged_kv(lens, hkv, d, 16, torch.float16, "cuda", layout="vllm", seed=2)
     q = torch.randn(n, hkv * group, d, device="cuda", dtype=torch.float16)
     k, v = fp8_caches(kv, "vllm", KS, VS)
