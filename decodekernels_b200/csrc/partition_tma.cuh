@@ -64,7 +64,9 @@ struct TmaConfig {
 // FP8: the caches hold e4m3 bytes (rows of D bytes, D / 128 column blocks);
 // the consumers convert in registers (tile_math_fp8.cuh).  SLICES: 16-token
 // slices per consumer warp and tile (2: the warp's two slices share one
-// softmax update, for the e4m3 path whose consumers bound the throughput).
+// softmax update, for the e4m3 path at head_dim 128 whose consumers bound the
+// throughput; the e4m3 path at 256 takes 1, for a ring small enough that
+// registers, not shared memory, bound the CTAs per SM).
 // MIN_CTAS: resident CTAs per SM the register allocation must allow (0: no
 // constraint, the compiler's own choice).  COMPACT: the grid is compact
 // (compact_coords) and a CTA runs items b, b + G, ..., carrying its ring
