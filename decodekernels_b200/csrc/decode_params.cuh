@@ -100,7 +100,17 @@ __device__ __forceinline__ void cta_coords(int num_partitions, int num_kv_heads,
 // 938 live CTAs of 8192).  An empty sequence keeps its partition-0 item (it
 // may write zeros).
 constexpr int kCompactMaxSeqs = 512;
+// The compact kernels are instantiated per lane capacity (sequences per
+// lane of the warp that scans the lengths): 4 for up to 128 sequences, 16 for
+// up to kCompactMaxSeqs.  The scans are unrolled over that capacity, and the
+// small instance's shorter code measured faster at every CTA's start (c4
+// 76.2 -> 75.3 us, c4f8 45.7 -> 44.2 us; the large one's prologue waited on
+// instruction fetch).
+constexpr int kCompactSmallPerLane = 4;
 constexpr int kCompactPerLane = kCompactMaxSeqs / 32;
+constexpr int compact_per_lane(int num_seqs) {
+  return num_seqs <= 32 * kCompactSmallPerLane ? kCompactSmallPerLane : kCompactPerLane;
+}
 
 // Item `target` of the compact numbering, computed by one warp (all 32 lanes):
 // lane l loads the lengths of sequences [l * per, (l + 1) * per) in one
@@ -111,23 +121,24 @@ constexpr int kCompactPerLane = kCompactMaxSeqs / 32;
 // fit_partition_size's choice).  STAGED: the lengths come from `staged`, the
 // clamped copy fit_partition_size left in shared memory, else from
 // p.seq_lens (one kind of load per instance, none issued speculatively).
-template <bool STAGED = false>
+// PER: the instance's lane capacity (num_seqs <= 32 * PER).
+template <int PER, bool STAGED = false>
 __device__ __forceinline__ bool compact_coords(const DecodeParams& p, const int* staged, unsigned target, int lane,
                                                int partition_size, int& part, int& kv_head, int& seq, int& seq_len) {
-  const int per = (p.num_seqs + 31) >> 5;  // <= kCompactPerLane
+  const int per = (p.num_seqs + 31) >> 5;  // <= PER
   const int first = lane * per;
   const unsigned ps = static_cast<unsigned>(partition_size);
   const unsigned hkv = static_cast<unsigned>(p.num_kv_heads);
-  int len[kCompactPerLane];
+  int len[PER];
 #pragma unroll
-  for (int j = 0; j < kCompactPerLane; ++j)
+  for (int j = 0; j < PER; ++j)
     len[j] = j < per && first + j < p.num_seqs
                  ? max(min(STAGED ? staged[first + j] : __ldg(p.seq_lens + first + j), p.max_seq_len), 0)
                  : -1;
-  unsigned parts[kCompactPerLane];
+  unsigned parts[PER];
   unsigned mine = 0;
 #pragma unroll
-  for (int j = 0; j < kCompactPerLane; ++j) {
+  for (int j = 0; j < PER; ++j) {
     parts[j] = 0;
     if (j >= per) continue;  // warp-uniform: no lane has a sequence here, and no division runs for it
     parts[j] = len[j] < 0 ? 0u : 1u;  // an empty sequence keeps one item
@@ -150,7 +161,7 @@ __device__ __forceinline__ bool compact_coords(const DecodeParams& p, const int*
     bool found = false;
     unsigned f_parts = 1;
 #pragma unroll
-    for (int j = 0; j < kCompactPerLane; ++j) {
+    for (int j = 0; j < PER; ++j) {
       const unsigned items = parts[j] * hkv;
       if (!found && r < items) {
         found = true;
@@ -210,6 +221,7 @@ __device__ __forceinline__ float* fit_size_slot(const DecodeParams& p) {
 // 128 (a power of two), so t <= 2^17 and 4 <= m <= 2^8.  Every CTA of a
 // launch computes the same value; CTA 0 leaves it in fit_size_slot for the
 // merge kernel.
+template <int PER>  // the instance's lane capacity (num_seqs <= 32 * PER)
 __device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* lens, int* best, int tid, int nthreads) {
   constexpr int K = 4;  // candidates per warp and round
   const int lane = tid & 31;
@@ -221,10 +233,10 @@ __device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* le
   if (tid == 0) *best = INT_MAX;
   for (int s = tid; s < p.num_seqs; s += nthreads) lens[s] = max(min(__ldg(p.seq_lens + s), p.max_seq_len), 0);
   __syncthreads();
-  uint32_t tiles[kCompactPerLane];
+  uint32_t tiles[PER];
   unsigned total = 0;
 #pragma unroll
-  for (int j = 0; j < kCompactPerLane; ++j) {
+  for (int j = 0; j < PER; ++j) {
     tiles[j] = 0;
     const int s = lane + 32 * j;
     if (j < nj && s < p.num_seqs) {
@@ -249,7 +261,7 @@ __device__ __forceinline__ int fit_partition_size(const DecodeParams& p, int* le
       n[k] = 0;
     }
 #pragma unroll
-    for (int j = 0; j < kCompactPerLane; ++j) {
+    for (int j = 0; j < PER; ++j) {
       if (j >= nj) break;
       if (lane + 32 * j < p.num_seqs) {
 #pragma unroll

@@ -605,7 +605,7 @@ int occupancy_of(Kernel kernel, int threads, int smem, int dev, bool* attr_done)
   return n;
 }
 
-template <typename T, int D, bool COMPACT>
+template <typename T, int D, int COMPACT>
 int tma_occupancy(bool fp8, int dev) {
   if (fp8) {
     if constexpr (D >= 128) {
@@ -628,9 +628,12 @@ int tma_occupancy(bool fp8, int dev) {
 // fitted partition size, the compact-grid instance whose one wave the device
 // fills).
 template <typename T, int D>
-int partition_occupancy(const DkPlan& pl, bool fp8, int dev) {
-  if (pl.path == DK_PATH_TMA_MMA)
-    return pl.fit_min_partition > 0 ? tma_occupancy<T, D, true>(fp8, dev) : tma_occupancy<T, D, false>(fp8, dev);
+int partition_occupancy(const DkPlan& pl, bool fp8, int num_seqs, int dev) {
+  if (pl.path == DK_PATH_TMA_MMA) {
+    if (pl.fit_min_partition == 0) return tma_occupancy<T, D, 0>(fp8, dev);
+    return compact_per_lane(num_seqs) == kCompactSmallPerLane ? tma_occupancy<T, D, kCompactSmallPerLane>(fp8, dev)
+                                                              : tma_occupancy<T, D, kCompactPerLane>(fp8, dev);
+  }
   static bool attr_done[kMaxDevices] = {false};
   return fp8 ? occupancy_of(paged_decode_simt_kernel<T, D, uint8_t>, kSimtThreads, SimtConfig<D>::kSmemBytes, dev,
                             attr_done)
@@ -643,13 +646,14 @@ int plan_occupancy(const DkPagedAttnArgs& a, const DkPlan& pl, int dev) {
   const bool fp8 = a.kv_fp8 != 0;
   switch (a.head_dim) {
     case 64:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 64>(pl, fp8, dev) : partition_occupancy<__half, 64>(pl, fp8, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 64>(pl, fp8, a.num_seqs, dev)
+                  : partition_occupancy<__half, 64>(pl, fp8, a.num_seqs, dev);
     case 128:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 128>(pl, fp8, dev)
-                  : partition_occupancy<__half, 128>(pl, fp8, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 128>(pl, fp8, a.num_seqs, dev)
+                  : partition_occupancy<__half, 128>(pl, fp8, a.num_seqs, dev);
     default:
-      return bf16 ? partition_occupancy<__nv_bfloat16, 256>(pl, fp8, dev)
-                  : partition_occupancy<__half, 256>(pl, fp8, dev);
+      return bf16 ? partition_occupancy<__nv_bfloat16, 256>(pl, fp8, a.num_seqs, dev)
+                  : partition_occupancy<__half, 256>(pl, fp8, a.num_seqs, dev);
   }
 }
 
@@ -672,9 +676,9 @@ unsigned compact_grid(Kernel kernel, int threads, int smem, int dev, int dense, 
   return static_cast<unsigned>(std::min<long long>(dense, 1LL * waves * cache[dev] * num_sms(dev)));
 }
 
-// One TMA partition kernel instance: e4m3 or 16-bit caches, dense or
-// compact grid.
-template <typename T, int D, bool FP8, bool COMPACT>
+// One TMA partition kernel instance: e4m3 or 16-bit caches, dense grid
+// (COMPACT 0) or compact grid of that lane capacity.
+template <typename T, int D, bool FP8, int COMPACT>
 int launch_tma(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int dev, cudaStream_t stream) {
   using Shape = std::conditional_t<FP8, TmaShapeFp8<D>, TmaShape<D>>;
   static bool attr_done[kMaxDevices] = {false};
@@ -686,7 +690,7 @@ int launch_tma(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, int 
   if (e != cudaSuccess)
     return fail_cuda(e, FP8 ? "cudaFuncSetAttribute(fp8 partition kernel)" : "cudaFuncSetAttribute(partition kernel)");
   dim3 grid(static_cast<unsigned>(pl.num_ctas));
-  if (COMPACT) {
+  if (COMPACT != 0) {
     // A fitted partition size puts every item in one wave when the lengths
     // allow it, and one wave of CTAs runs them; the CTAs loop over the items
     // when they do not.
@@ -708,15 +712,19 @@ int launch_typed(const DkPagedAttnArgs& a, const DkPlan& pl, DecodeParams& p, in
   cudaError_t e;
   if (pl.path == DK_PATH_TMA_MMA && p.kv_fp8) {
     if constexpr (D >= 128) {  // e4m3 rows of at least one 128-byte block (the planner's rule)
-      const int r = p.compact ? launch_tma<T, D, true, true>(a, pl, p, dev, stream)
-                              : launch_tma<T, D, true, false>(a, pl, p, dev, stream);
+      const int r = !p.compact ? launch_tma<T, D, true, 0>(a, pl, p, dev, stream)
+                    : compact_per_lane(a.num_seqs) == kCompactSmallPerLane
+                        ? launch_tma<T, D, true, kCompactSmallPerLane>(a, pl, p, dev, stream)
+                        : launch_tma<T, D, true, kCompactPerLane>(a, pl, p, dev, stream);
       if (r) return r;
     } else {
       return fail(1, "internal: fp8 TMA path planned for head_dim %d", D);
     }
   } else if (pl.path == DK_PATH_TMA_MMA) {
-    const int r = p.compact ? launch_tma<T, D, false, true>(a, pl, p, dev, stream)
-                            : launch_tma<T, D, false, false>(a, pl, p, dev, stream);
+    const int r = !p.compact ? launch_tma<T, D, false, 0>(a, pl, p, dev, stream)
+                  : compact_per_lane(a.num_seqs) == kCompactSmallPerLane
+                      ? launch_tma<T, D, false, kCompactSmallPerLane>(a, pl, p, dev, stream)
+                      : launch_tma<T, D, false, kCompactPerLane>(a, pl, p, dev, stream);
     if (r) return r;
   } else if (p.kv_fp8) {
     auto kernel = paged_decode_simt_kernel<T, D, uint8_t>;

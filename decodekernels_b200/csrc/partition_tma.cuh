@@ -68,12 +68,13 @@ struct TmaConfig {
 // throughput; the e4m3 path at 256 takes 1, for a ring small enough that
 // registers, not shared memory, bound the CTAs per SM).
 // MIN_CTAS: resident CTAs per SM the register allocation must allow (0: no
-// constraint, the compiler's own choice).  COMPACT: the grid is compact
-// (compact_coords) and a CTA runs items b, b + G, ..., carrying its ring
-// position and barrier phases from item to item; otherwise one CTA per
-// (partition, kv_head, seq) of the dense grid (cta_coords).
+// constraint, the compiler's own choice).  COMPACT > 0: the grid is compact
+// (compact_coords; COMPACT is the lane capacity of its length scans,
+// kCompactSmallPerLane or kCompactPerLane) and a CTA runs items b, b + G, ...,
+// carrying its ring position and barrier phases from item to item; 0: one CTA
+// per (partition, kv_head, seq) of the dense grid (cta_coords).
 template <typename T, int D, int NSTAGES, int WARPS, bool FP8 = false, int SLICES = 1, int MIN_CTAS = 0,
-          bool COMPACT = false>
+          int COMPACT = 0>
 __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     paged_decode_tma_kernel(const __grid_constant__ CUtensorMap k_map, const __grid_constant__ CUtensorMap v_map,
                             const DecodeParams p) {
@@ -91,7 +92,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
   __shared__ int s_abort;    // compact grid: a bounded wait gave up, so run no further item
 
   int part = 0, kv_head = 0, seq = 0;
-  if constexpr (!COMPACT) cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
+  if constexpr (COMPACT == 0) cta_coords(p.num_partitions, p.num_kv_heads, part, kv_head, seq);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int rows_log2 = p.rows_log2;
@@ -106,7 +107,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
       mbar_init(&empty_bar[s], WARPS);
     }
     mbar_init_fence();
-    if constexpr (COMPACT) s_abort = 0;
+    if constexpr (COMPACT != 0) s_abort = 0;
   }
   if (warp == WARPS && lane == 0) {
     tma_prefetch_desc(&k_map);
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
   // fit_partition_size's choice when p.fit_slots > 0.  Read where it is used
   // (per item, not in the tile loop) so that it holds no register across it.
   auto part_size = [&]() -> int {
-    if constexpr (COMPACT)
+    if constexpr (COMPACT != 0)
       return *static_cast<volatile int*>(&s_ps);
     else
       return p.partition_size;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
         const uint32_t u = g0 + t;
         const int s = static_cast<int>(u % NSTAGES);
         if (!mbar_wait(&empty_bar[s], ((u / NSTAGES) & 1) ^ 1)) {
-          if constexpr (COMPACT) s_abort = 1;
+          if constexpr (COMPACT != 0) s_abort = 1;
           break;
         }
         const int tstart = pstart + t * TILE;
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
       // item arrives after this one, below.)
       if (sub0 >= pend) break;
       if (!mbar_wait(&full_bar[s], (u / NSTAGES) & 1)) {
-        if constexpr (COMPACT) s_abort = 1;
+        if constexpr (COMPACT != 0) s_abort = 1;
         break;
       }
       if constexpr (SLICES == 2)
@@ -221,7 +222,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     named_bar_sync(1, Cfg::kThreads);
     write_partition_result<T, D, WARPS>(p, red, seq, kv_head, part, seq_len, part_size(), threadIdx.x,
                                         Cfg::kThreads, [] { named_bar_sync(1, Cfg::kThreads); });
-    if constexpr (COMPACT) {
+    if constexpr (COMPACT != 0) {
       // A warp with no rows in the last tile arrives on its empty barrier now,
       // when every warp has finished reading the ring (the epilogue's
       // barriers), so that the stage's phase completes before the next item.
@@ -239,7 +240,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     }
   };
 
-  if constexpr (!COMPACT) {
+  if constexpr (COMPACT == 0) {
     int pb = 0, off = 0;  // this lane's page of the next tile: block id and first row in the block
     first_page(part, seq, pb, off);
     const int seq_len = min(p.seq_lens[seq], p.max_seq_len);  // lengths above max_seq_len count as max_seq_len
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
     // call, readable after the grid-dependency wait above).
     bool from_ring = false;
     if (FP8 && p.fit_slots > 0) {
-      const int ps = fit_partition_size(p, reinterpret_cast<int*>(smem), &s_fit, threadIdx.x, Cfg::kThreads);
+      const int ps = fit_partition_size<COMPACT>(p, reinterpret_cast<int*>(smem), &s_fit, threadIdx.x, Cfg::kThreads);
       from_ring = true;
       if (threadIdx.x == 0) {
         s_ps = ps;
@@ -275,10 +276,10 @@ __global__ void __launch_bounds__((WARPS + 1) * 32, MIN_CTAS)
         bool live;
         if constexpr (FP8) {
           const int* staged = reinterpret_cast<const int*>(smem);
-          live = from_ring ? compact_coords<true>(p, staged, item, lane, part_size(), part, kv_head, seq, len)
-                           : compact_coords(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
+          live = from_ring ? compact_coords<COMPACT, true>(p, staged, item, lane, part_size(), part, kv_head, seq, len)
+                           : compact_coords<COMPACT>(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
         } else {
-          live = compact_coords(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
+          live = compact_coords<COMPACT>(p, nullptr, item, lane, part_size(), part, kv_head, seq, len);
         }
         if (from_ring) {
           // the ring's first TMA writes follow: order these reads of it before them

@@ -103,11 +103,12 @@ def test_persistent_repeated_calls_identical():
     assert capi.wait_timeouts(0) == 0
 
 
-@pytest.mark.parametrize("n", [512, 513])
+@pytest.mark.parametrize("n", [128, 129, 512, 513])
 def test_compact_grid_at_its_sequence_limit(n):
-    """512 sequences: the warp scan's largest batch (16 lengths per lane); 513
-    falls back to the dense grid.  Both agree bit for bit with the dense grid
-    and match the oracle on a sample of sequences."""
+    """128 sequences: the small compact instance's largest batch (4 lengths
+    per lane); 129 takes the large one; 512: its largest batch (16 lengths
+    per lane); 513 falls back to the dense grid.  All agree bit for bit with
+    the dense grid and match the oracle on a sample of sequences."""
     g = torch.Generator().manual_seed(n)
     lens = torch.randint(0, 1200, (n,), generator=g).tolist()
     kv = make_paged_kv(lens, 1, 128, 16, torch.bfloat16, "cuda", layout="nhd", seed=n)
